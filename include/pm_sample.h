@@ -1,0 +1,177 @@
+/*
+ * pm_sample.h -- C ABI of the B200 token-selection path (libpm_sample.so).
+ *
+ * Replaces the per-step token selection of PagedMoE's decode loop: the
+ * logits processors, the log-softmax, the sampler and the draft acceptance
+ * of a verify pass.  All pointers are device pointers unless stated; every
+ * function takes a cudaStream_t (as void*) and returns a status code, never
+ * aborts, allocates nothing, and keeps no global state, so it may be called
+ * from several host threads on different streams with separate workspaces.
+ *
+ * Reference interfaces replaced (paths within noahclark556/paged-moe):
+ *   pm_sample_rows      sampler(logprobs) -> tokens, built by mlx-lm's
+ *                       make_sampler (call sites pagedmoe/verify_decode.py:839,
+ *                       :903, pagedmoe/lookup_decode.py:359, run.py:53) plus
+ *                       the processor loop before it (verify_decode.py:828-835,
+ *                       :889-899) fused into one pass over the logits.
+ *   pm_apply_processors proc(tokens, logits) -> logits, built by mlx-lm's
+ *                       make_logits_processors (verify_decode.py:830-831,
+ *                       :895-896; lookup_decode.py:344-356), and the
+ *                       where(mask, x, -inf) processors of
+ *                       pagedmoe/think_budget.py:107-109 and rescue.py:240-245.
+ *   pm_logprobs         logits - logsumexp(logits) (verify_decode.py:835, :899;
+ *                       lookup_decode.py:358).
+ *   pm_verify           the accept loop of a verify pass
+ *                       (lookup_decode.py:363-369, verify_decode.py:903-921),
+ *                       plus residual rejection sampling (no reference code).
+ *   pm_shard_summarize / pm_shard_merge
+ *                       vocab-sharded sampling (no reference code: the
+ *                       reference runs on one device).
+ */
+#ifndef PM_SAMPLE_H
+#define PM_SAMPLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PM_API __attribute__((visibility("default")))
+#else
+#define PM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define PM_OK 0
+#define PM_ERR_ARG (-1)          /* bad argument (null pointer, bad size, ...) */
+#define PM_ERR_CUDA (-2)         /* a CUDA call failed; see pm_last_cuda_error */
+#define PM_ERR_UNSUPPORTED (-3)  /* valid but outside this build's limits */
+#define PM_ERR_WORKSPACE (-4)    /* workspace smaller than pm_*_workspace_bytes */
+
+/* logits element types */
+#define PM_DTYPE_F32 0
+#define PM_DTYPE_BF16 1
+
+/* noise sources */
+#define PM_NOISE_PHILOX 0   /* Philox4x32-10 keyed by (seed, offset, row) */
+#define PM_NOISE_INJECTED 1 /* caller-provided Gumbel values and uniforms */
+
+/* pm_row_params.flags */
+#define PM_F_GREEDY 0x1u    /* temperature == 0: argmax */
+#define PM_F_TOP_P 0x2u     /* 0 < top_p < 1 */
+#define PM_F_MIN_P 0x4u     /* min_p != 0 */
+#define PM_F_REP 0x10u      /* repetition penalty on */
+#define PM_F_PRES 0x20u     /* presence penalty on */
+#define PM_F_FREQ 0x40u     /* frequency penalty on */
+#define PM_F_UNBOUNDED 0x100u /* top_p or min_p on while top_k is off */
+#define PM_F_FULL 0x200u    /* temperature > 0 and no filter: whole-vocabulary draw */
+
+/* Per-row sampling and processor settings.  Scalars are the fp32 values the
+ * reference's arithmetic sees: inv_temperature = fl32(1/temp),
+ * top_p_comp = fl32(1 - top_p), log_min_p = fl32(log(min_p)), evaluated in
+ * double first as Python does (mlx-lm make_sampler / make_logits_processors
+ * keyword arguments; defaults resolved by pagedmoe/sampling.py:121-135). */
+typedef struct pm_row_params {
+    uint32_t flags;
+    float inv_temperature;
+    int32_t top_k;               /* <= 0: off */
+    float top_p_comp;
+    float log_min_p;
+    int32_t min_tokens_to_keep;
+    float repetition_penalty;
+    int32_t repetition_context_size;
+    float presence_penalty;
+    int32_t presence_context_size;
+    float frequency_penalty;
+    int32_t frequency_context_size;
+} pm_row_params;
+
+/* Rows of logits plus the processors that act on them. */
+typedef struct pm_rows {
+    const void *logits;          /* [rows, row_stride] of dtype */
+    int32_t dtype;               /* PM_DTYPE_* */
+    int64_t rows;
+    int64_t vocab;
+    int64_t row_stride;          /* elements between rows (>= vocab) */
+    const pm_row_params *params; /* [rows], or [1] when params_per_row == 0 */
+    int32_t params_per_row;
+    /* history the penalties read.  Without feed, row r uses
+     * hist[r, 0:hist_len[r]].  With feed (a verify pass), row r belongs to
+     * request b = r / feed_group at position i = r % feed_group and uses
+     * hist[b, 0:hist_len[b]] followed by feed[b, 0:i+1], i.e. its history plus
+     * [y] + drafts[:i] (reference verify_decode.py:889-898). */
+    const int32_t *hist;         /* [hist_rows, hist_stride] or NULL */
+    const int32_t *hist_len;     /* [hist_rows] or NULL (all hist_stride) */
+    int64_t hist_stride;
+    const int32_t *feed;         /* [rows / feed_group, feed_group] or NULL */
+    int32_t feed_group;          /* rows per request when feed != NULL */
+    /* logit bias shared by all rows (mlx-lm logit_bias) */
+    const int32_t *bias_tokens;  /* [n_bias] distinct ids, ascending */
+    const float *bias_values;    /* [n_bias] */
+    int32_t n_bias;
+    /* allowed-token bitmask: bit v of word v/32 of row r; NULL = all allowed */
+    const uint32_t *mask;        /* [rows, mask_stride] */
+    int64_t mask_stride;         /* words, >= ceil(vocab / 32) */
+    /* host-side bounds of the device params (they size the launch): the OR of
+     * every row's flags, and the largest top_k of any row (0 if none). */
+    uint32_t flags_any;
+    int32_t top_k_max;
+} pm_rows;
+
+/* Noise of the draw. */
+typedef struct pm_noise {
+    int32_t mode;                /* PM_NOISE_* */
+    uint64_t seed;
+    uint64_t offset;             /* advances per step */
+    uint32_t row_base;           /* Philox row id of row 0 */
+    const float *gumbel;         /* injected: [rows, gumbel_stride] Gumbel values */
+    int64_t gumbel_stride;
+    const double *uniform;       /* injected: [rows, 2] uniforms in [0,1) */
+} pm_noise;
+
+/* Outputs of pm_sample_rows (only tokens is required). */
+typedef struct pm_sample_out {
+    int32_t *tokens;             /* [rows] */
+    float *lse;                  /* [rows] row log-sum-exp of the processed logits, or NULL */
+    float *token_logprob;        /* [rows] logprob of the chosen token, or NULL */
+    int32_t *surv_ids;           /* [rows, surv_cap] survivors in rank order, or NULL */
+    float *surv_probs;           /* [rows, surv_cap] their probabilities at temperature */
+    int32_t *n_surv;             /* [rows] */
+    int32_t surv_cap;
+} pm_sample_out;
+
+/* Workspace bytes pm_sample_rows needs for these rows.  The workspace must be
+ * zero-filled before its first use; every call leaves it ready for the next. */
+PM_API size_t pm_sample_workspace_bytes(const pm_rows *rows);
+
+/* One fused pass: processors, row log-sum-exp, top-k / top-p / min-p,
+ * temperature and the draw, for every row.  Replaces mlx-lm's
+ * make_sampler(...)(logprobs) after make_logits_processors(...) processors
+ * (reference verify_decode.py:828-839). */
+PM_API int pm_sample_rows(const pm_rows *rows, const pm_noise *noise, const pm_sample_out *out,
+                   void *workspace, size_t workspace_bytes, void *stream);
+
+/* Processed logits [rows, vocab] fp32 (logit bias, penalties, mask), the
+ * callables of make_logits_processors (verify_decode.py:830-831). */
+PM_API size_t pm_processors_workspace_bytes(const pm_rows *rows);
+PM_API int pm_apply_processors(const pm_rows *rows, float *out, int64_t out_stride, void *workspace,
+                        size_t workspace_bytes, void *stream);
+
+/* Processed logits minus their row log-sum-exp (verify_decode.py:835). */
+PM_API int pm_logprobs(const pm_rows *rows, float *out, int64_t out_stride, float *lse_out, void *workspace,
+                size_t workspace_bytes, void *stream);
+
+/* Last CUDA error seen by this thread (cudaError_t value), 0 if none. */
+PM_API int pm_last_cuda_error(void);
+
+/* Library version string. */
+PM_API const char *pm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PM_SAMPLE_H */

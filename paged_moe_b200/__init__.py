@@ -1,0 +1,30 @@
+"""B200-native token selection for PagedMoE's decode loop.
+
+Public API:
+    make_sampler, make_logits_processors   drop-ins for mlx-lm's factories
+    sample_rows, apply_processors, logprobs batched fast paths ([B, V] at once)
+    verify                                  draft acceptance of a verify pass
+    sampling                                request defaults (pagedmoe/sampling.py)
+
+Importing this package loads libpm_sample.so; there is no CPU path.
+"""
+
+from . import _lib
+from . import sampling  # noqa: F401  (host-side defaults, pure Python)
+from .params import ProcessorSettings, SamplerSettings  # noqa: F401
+
+_lib.load()
+
+from .engine import apply_processors, logprobs, sample_rows  # noqa: E402,F401
+from .sample_utils import make_logits_processors, make_sampler  # noqa: E402,F401
+
+try:  # verify / sharding live in their own modules
+    from .verify import verify  # noqa: E402,F401
+except ImportError:  # pragma: no cover - during bring-up only
+    pass
+
+__version__ = "0.1.0"
+
+
+def library_path() -> str:
+    return _lib._build.SO
