@@ -1,0 +1,335 @@
+"""Benchmark of the fused token-selection pass (one JSON line on rank 0).
+
+Workload (the one the headline metric is quoted on):
+B=256 rows per GPU, V=163,840 fp32 logits N(0,1)*2 + 9 at 64 ids per row, a
+packed allowed-token bitmask (~2% of bits: 4 blocks of 512 + ~1,200
+singletons), temp 1.0, top_k 50, top_p 0.95, Philox Gumbel-max draw.
+
+A step is one pm_sample_rows call over one batch.  `value` is whole-job rows/s
+with inputs resident in HBM; `e2e` is the same metric through the public API
+with pinned host buffers copied in and tokens copied out inside the timed
+region.  Two input batches alternate so that no step finds its logits in L2
+(each batch is 173 MB, the L2 126 MB).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "sampled rows/s at B=256,V=152k; logits HBM GB/s vs peak; p50 µs/step"
+B_PER_GPU = 256
+VOCAB = 163840
+BYTES_PER_ROW = VOCAB * 4 + (VOCAB // 32) * 4  # logits + bitmask = 675,840 B
+WORKLOAD = ("C3: 256 rows per GPU, V=163,840 fp32 logits + packed allowed-token bitmask (~2% set), "
+            "temp 1.0, top_k 50, top_p 0.95, Philox Gumbel-max draw")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_per_launch():
+    """DRAM bytes per launch from the committed ncu summary (None if absent)."""
+    path = os.path.join(ROOT, "profiles", "k_sample_stream_c3.md")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    mx = float(f[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, f[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        except OSError:
+            pass
+        finally:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(seed: int):
+    from paged_moe_b200 import workloads as W
+    d = W.c3(seed=seed, B=B_PER_GPU, V=VOCAB)
+    return d
+
+
+def cpu_baseline(d, seconds: float):
+    """The oracle (C restatement of the reference path) on all host cores over
+    a bounded sample of the same workload: whole steps of 256 rows, repeated
+    until `seconds` of wall time has passed (at least one)."""
+    import numpy as np
+
+    import oracle as O
+    s = d["sampler"]
+    osamp = O.Sampler(temp=s.temp, top_p=s.top_p, top_k=s.top_k)
+    cores = os.cpu_count() or 1
+    O.lib()
+    rows = 0
+    t0 = time.perf_counter()
+    steps = 0
+    while True:
+        O.sample(d["logits"], osamp, mask=d["mask"], seed=1, offset=steps, nthreads=cores)
+        rows += d["logits"].shape[0]
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or steps >= 64:
+            break
+    return {"value": rows / el, "unit": "rows/s", "cores": cores, "kind": "port",
+            "sample": f"{steps} full C3 steps x {d['logits'].shape[0]} rows, {el:.1f} s wall"}
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import numpy as np  # noqa: F401
+
+    import oracle as O
+    d = make_inputs(seed=0)
+    s = d["sampler"]
+    osamp = O.Sampler(temp=s.temp, top_p=s.top_p, top_k=s.top_k)
+    cores = os.cpu_count() or 1
+    # each step is the full 256-row batch (about 0.1 s on 8 cores)
+    n = B_PER_GPU
+    x, m = d["logits"][:n], d["mask"][:n]
+    for i in range(args.warmup):
+        O.sample(x, osamp, mask=m, seed=1, offset=i, nthreads=cores)
+    times = []
+    for i in range(args.steps):
+        t0 = time.perf_counter()
+        O.sample(x, osamp, mask=m, seed=1, offset=1000 + i, nthreads=cores)
+        times.append(time.perf_counter() - t0)
+    tot = sum(times)
+    val = n * args.steps / tot
+    line = {
+        "metric": METRIC, "value": val, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * tot / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "rows_per_step": n, "vocab": VOCAB},
+        "impl": "reference",
+        "cpu_baseline": {"value": val, "unit": "rows/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} C3 rows per step, oracle on {cores} host threads "
+                                   "(the reference's MLX path is darwin-only)"},
+        "e2e": {"value": val, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    rank, world, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        pg = dist
+    import paged_moe_b200 as pm
+
+    d0 = make_inputs(seed=1000 * rank)
+    d1 = make_inputs(seed=1000 * rank + 1)
+    s = d0["sampler"]
+    xs = [torch.from_numpy(d["logits"]).to(dev) for d in (d0, d1)]
+    ms = [torch.from_numpy(d["mask"].view(np.int32)).to(dev) for d in (d0, d1)]
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        return pm.sample_rows(xs[i & 1], s, mask=ms[i & 1], seed=12345, offset=i, row_base=rank * B_PER_GPU)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize(dev)
+    with Clocks(dev.index if world == 1 else local) as clk:
+        ev[0].record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize(dev)
+    clocks = clk.summary()
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    total_ms = ev[0].elapsed_time(ev[-1])
+    if pg:
+        t = torch.tensor([total_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        total_ms = float(t.item())
+        pg.barrier()
+    ms_step = total_ms / args.steps
+    rows_total = B_PER_GPU * world
+    value = rows_total / (ms_step / 1000.0)
+
+    # end to end through the public API: pinned host logits + mask in, tokens out
+    hx = [torch.from_numpy(d["logits"]).pin_memory() for d in (d0, d1)]
+    hm = [torch.from_numpy(d["mask"].view(np.int32)).pin_memory() for d in (d0, d1)]
+    htok = torch.empty(B_PER_GPU, dtype=torch.int32).pin_memory()
+    dx = torch.empty_like(xs[0])
+    dm = torch.empty_like(ms[0])
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step(i):
+        dx.copy_(hx[i & 1], non_blocking=True)
+        dm.copy_(hm[i & 1], non_blocking=True)
+        out = pm.sample_rows(dx, s, mask=dm, seed=777, offset=i, row_base=rank * B_PER_GPU)
+        htok.copy_(out["tokens"], non_blocking=True)
+
+    for i in range(2):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    if pg:
+        pg.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if pg:
+        t = torch.tensor([e2e_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_val = rows_total / (e2e_ms / e2e_steps / 1000.0)
+    h2d = hx[0].numel() * 4 + hm[0].numel() * 4
+    d2h = htok.numel() * 4
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(d0, args.cpu_seconds)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank != 0:
+        return
+    peak, peak_kind = peaks()
+    bytes_launch = BYTES_PER_ROW * B_PER_GPU
+    mean_launch_s = statistics.mean(per) / 1000.0
+    achieved = bytes_launch / mean_launch_s / 1e9
+    trf = traffic_per_launch()
+    line = {
+        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "rows_per_gpu": B_PER_GPU, "vocab": VOCAB,
+                   "l2": "two alternating input batches of 173 MB each (> 126 MB L2)",
+                   "noise": "Philox4x32-10"},
+        "p50_us_per_step": 1000 * statistics.median(per),
+        "logits_gb_per_s": achieved,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": trf,
+                     "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs",
+                     "algorithmic_bytes_per_launch": bytes_launch},
+        "e2e": {"value": e2e_val, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

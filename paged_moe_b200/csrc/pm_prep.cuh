@@ -65,10 +65,8 @@ __global__ void __launch_bounds__(1024) k_prep_overrides(PrepArgs a) {
   int s = s_rep < s_pres ? s_rep : s_pres;
   s = s < s_freq ? s : s_freq;
   int n = H - s;
-  if (n > a.cap) {
-    if (tid == 0) a.status[r] = 2;  // window longer than this build's history cap
-    n = 0;
-  }
+  if (tid == 0) a.status[r] = n > a.cap ? 2 : 0;  // 2: window longer than this build's history cap
+  if (n > a.cap) n = 0;
   // load (id << 32 | position); ids outside [0, V) sort last and are dropped
   for (int i = tid; i < a.cap; i += nth) {
     uint64_t k = ~0ull;

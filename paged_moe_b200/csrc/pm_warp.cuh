@@ -1,0 +1,449 @@
+// pm_warp.cuh -- warp-level pieces of the streaming kernels: the candidate
+// buffer behind a running threshold, the exact row log-sum-exp from tile
+// statistics, the filters and the draws.  Each function is called by one
+// full warp and uses only that warp's shared memory.
+#pragma once
+
+#include "pm_device.cuh"
+#include "pm_select.cuh"
+#include "pm_tile.cuh"
+
+namespace pm {
+
+// Candidate buffer state of one warp (identical in every lane).
+struct Cand {
+  int cnt;
+  uint64_t tau;   // smallest key kept by the last compaction (0: none yet)
+  float tau_x;    // its value, for the cheap pre-test
+  bool trimmed;   // a compaction dropped keys
+};
+
+__device__ __forceinline__ void cand_reset(Cand& c) {
+  c.cnt = 0;
+  c.tau = 0;
+  c.tau_x = -INFINITY;
+  c.trimmed = false;
+}
+
+// Keep the K largest of buf[0..cnt) (cnt > K); returns the smallest kept key.
+// Out of line and by value, so the caller's buffer state stays in registers.
+template <int CAP>
+__device__ __noinline__ uint64_t compact_keys(uint64_t* buf, unsigned* hist, int cnt, int K) {
+  return warp_select_topk<(CAP + 31) / 32>(buf, cnt, K, hist);
+}
+
+template <int CAP>
+__device__ __forceinline__ void cand_compact(uint64_t* buf, unsigned* hist, Cand& c, int K) {
+  c.tau = compact_keys<CAP>(buf, hist, c.cnt, K);
+  c.tau_x = key_value(c.tau);
+  c.cnt = K;
+  c.trimmed = true;
+}
+
+// Offer one value per lane (token tok) to the buffer: appended when its key
+// beats the threshold.  The common case costs one compare and one vote.
+template <int CAP>
+__device__ __forceinline__ void cand_offer_one(float x, uint32_t tok, uint64_t* buf, unsigned* hist, Cand& c,
+                                               int K) {
+  const int lane = threadIdx.x & 31;
+  const bool pre = x > -INFINITY && x >= c.tau_x;
+  if (!__any_sync(kFull, pre)) return;
+  const uint64_t key = rankkey(x, tok);
+  const bool ok = pre && key > c.tau;
+  const unsigned bal = __ballot_sync(kFull, ok);
+  if (ok) buf[c.cnt + __popc(bal & ((1u << lane) - 1u))] = key;
+  c.cnt += __popc(bal);
+  __syncwarp();
+  if (c.cnt > CAP - 32) cand_compact<CAP>(buf, hist, c, K);
+}
+
+// Offer one key per lane (0 = nothing).
+template <int CAP>
+__device__ __forceinline__ void cand_offer_key(uint64_t key, uint64_t* buf, unsigned* hist, Cand& c, int K) {
+  const int lane = threadIdx.x & 31;
+  const bool ok = key != 0ull && key > c.tau;
+  const unsigned bal = __ballot_sync(kFull, ok);
+  if (!bal) return;
+  if (ok) buf[c.cnt + __popc(bal & ((1u << lane) - 1u))] = key;
+  c.cnt += __popc(bal);
+  __syncwarp();
+  if (c.cnt > CAP - 32) cand_compact<CAP>(buf, hist, c, K);
+}
+
+// Bitonic sort of S[0..m) descending by one warp (P = power of two >= m, <= cap).
+__device__ __forceinline__ void warp_sort_desc(uint64_t* S, int m) {
+  const int lane = threadIdx.x & 31;
+  int P = 1;
+  while (P < m) P <<= 1;
+  for (int i = m + lane; i < P; i += 32) S[i] = 0ull;
+  __syncwarp();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = lane; i < P; i += 32) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint64_t x = S[i], y = S[ixj];
+          const bool desc = (i & k) == 0;
+          if (desc ? (x < y) : (x > y)) { S[i] = y; S[ixj] = x; }
+        }
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// a_t = s_t e^(m_t - m) of tile t (0 for an empty tile).
+__device__ __forceinline__ double tile_weight(const TileStat* st, int t, float m) {
+  const uint64_t s = ld_cg(&st[t].s);
+  if (!s) return 0.0;
+  return dmul((double)s, det_exp64(dsub((double)ld_cg(&st[t].m), (double)m)));
+}
+
+// Row log-sum-exp from its tile statistics, one warp:
+//   m = max_t m_t,  Z = pairwise sum over t of s_t e^(m_t - m)  (tiles padded
+//   with zeros to a power of two; lane L sums its contiguous block of P/32
+//   tiles as a complete subtree, then the lanes combine pairwise),
+//   c = fl32(m + log(Z 2^-52)).  -inf when no tile has a finite value.
+__device__ __forceinline__ float warp_combine(const TileStat* st, int nt, float* m_out) {
+  const int lane = threadIdx.x & 31;
+  float m = -INFINITY;
+  for (int t = lane; t < nt; t += 32) m = fmaxf(m, ld_cg(&st[t].m));
+  m = warp_max(m);
+  *m_out = m;
+  if (!(m > -INFINITY)) return -INFINITY;
+  int P = 32;
+  while (P < nt) P <<= 1;
+  const int per = P >> 5;
+  double stk[12];
+  int sp = 0;
+  for (int i = 0; i < per; ++i) {
+    const int t = lane * per + i;
+    double v = t < nt ? tile_weight(st, t, m) : 0.0;
+    for (int c = i + 1; (c & 1) == 0; c >>= 1) v = dadd(stk[--sp], v);
+    stk[sp++] = v;
+  }
+  double acc = stk[0];
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_down_sync(kFull, acc, o);
+    if ((lane & (2 * o - 1)) == 0) acc = dadd(acc, t);
+  }
+  const double Z = __shfl_sync(kFull, acc, 0);
+  return (float)dadd((double)m, det_log64(dmul(Z, 0x1p-52)));
+}
+
+__device__ __forceinline__ float row_gumbel(const SampleArgs& a, int64_t row, uint32_t token) {
+  if (a.noise_mode == PM_NOISE_INJECTED) return a.gumbel[row * a.gumbel_stride + token];
+  return philox_gumbel(a.seed, a.offset, a.row_base + (uint32_t)row, token);
+}
+
+__device__ __forceinline__ uint64_t row_u53(const SampleArgs& a, int64_t row, int stream) {
+  if (a.noise_mode == PM_NOISE_INJECTED) return u53_from_double(a.uniform[row * 2 + stream]);
+  return philox_u53(a.seed, a.offset, a.row_base + (uint32_t)row, (uint32_t)stream);
+}
+
+// The sampler's filters over the row's sorted top candidates S[0..m) and the
+// Gumbel-max draw (mlx-lm make_sampler chain: top_k, top_p, min_p, then the
+// categorical at temperature).
+//   top_p: keep rank r while T - A_r > Q(1 - top_p), A_r the exclusive prefix
+//          of q52(x - c) in rank order, T their sum when top_k is on, else 2^52;
+//   min_p: drop ranks >= min_tokens_to_keep with fl32(x - c) <
+//          fl32(fl32(x_0 - c) + log(min_p));
+//   draw:  argmax over survivors of fl32(fl32(x * inv_temp) + g), ties to the
+//          lowest id.
+// Returns the token, or -1 when the survivors reach past the candidates (the
+// row is then flagged; only possible when top_k is off).  *n_out = survivors.
+__device__ int warp_filter_draw(const SampleArgs& a, const pm_row_params& p, int64_t row, const uint64_t* S,
+                                int m, bool complete, float c, int* n_out) {
+  const int lane = threadIdx.x & 31;
+  *n_out = 0;
+  if (m == 0) return 0;
+  const bool topk = p.top_k > 0;
+  int cnt = (topk && p.top_k < m) ? p.top_k : m;
+  bool determined = topk || complete;
+  if (p.flags & PM_F_TOP_P) {
+    uint64_t T = 0;
+    for (int r = lane; r < cnt; r += 32) T += q52(fsub(key_value(S[r]), c));
+    T = warp_sum_u64(T);
+    if (!topk) T = 1ull << 52;
+    const uint64_t qthr = __float2ull_rz(fmul(p.top_p_comp, 0x1p52f));
+    uint64_t carry = 0;
+    int keep = cnt;
+    bool found = false;
+    for (int base = 0; base < cnt && !found; base += 32) {
+      const int r = base + lane;
+      const uint64_t q = r < cnt ? q52(fsub(key_value(S[r]), c)) : 0ull;
+      const uint64_t incl = warp_incl_scan_u64(q);
+      const uint64_t A = carry + incl - q;
+      const bool ok = r < cnt && A < T && (T - A) > qthr;
+      const unsigned fail = __ballot_sync(kFull, r < cnt && !ok);
+      if (fail) { keep = base + __ffs(fail) - 1; found = true; }
+      carry += __shfl_sync(kFull, incl, 31);
+    }
+    if (found) determined = true;
+    cnt = keep < 1 ? 1 : keep;
+  }
+  if (p.flags & PM_F_MIN_P) {
+    const float thr = fadd(fsub(key_value(S[0]), c), p.log_min_p);
+    int keep = cnt;
+    bool found = false;
+    for (int base = 0; base < cnt && !found; base += 32) {
+      const int r = base + lane;
+      const bool drop = r < cnt && r >= p.min_tokens_to_keep && fsub(key_value(S[r]), c) < thr;
+      const unsigned bal = __ballot_sync(kFull, drop);
+      if (bal) { keep = base + __ffs(bal) - 1; found = true; }
+    }
+    if (found) determined = true;
+    cnt = keep < 1 ? 1 : keep;
+  }
+  if (!determined) return -1;
+  float bs = -INFINITY;
+  int bid = -1;
+  for (int r = lane; r < cnt; r += 32) {
+    const uint32_t id = key_index(S[r]);
+    const float sc = fadd(fmul(key_value(S[r]), p.inv_temperature), row_gumbel(a, row, id));
+    if (bid < 0 || sc > bs || (sc == bs && (int)id < bid)) { bs = sc; bid = (int)id; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float os = __shfl_xor_sync(kFull, bs, o);
+    const int oid = __shfl_xor_sync(kFull, bid, o);
+    if (oid >= 0 && (bid < 0 || os > bs || (os == bs && oid < bid))) { bs = os; bid = oid; }
+  }
+  *n_out = cnt;
+  return bid;
+}
+
+// Renormalised survivor probabilities at temperature (fp64, rank order,
+// sequential sum) into the row's output slots.  Lane 0.
+__device__ __noinline__ void write_survivors(const SampleArgs& a, const pm_row_params& p, int64_t row,
+                                                const uint64_t* S, int cnt) {
+  double ymax = -INFINITY;
+  for (int r = 0; r < cnt; ++r) {
+    const double yv = (double)fmul(key_value(S[r]), p.inv_temperature);
+    ymax = yv > ymax ? yv : ymax;
+  }
+  double Z = 0.0;
+  for (int r = 0; r < cnt; ++r) Z = dadd(Z, det_exp64(dsub((double)fmul(key_value(S[r]), p.inv_temperature), ymax)));
+  int32_t* ids = a.surv_ids + row * a.surv_cap;
+  float* prs = a.surv_probs + row * a.surv_cap;
+  for (int r = 0; r < a.surv_cap; ++r) {
+    if (r < cnt) {
+      ids[r] = (int32_t)key_index(S[r]);
+      prs[r] = (float)__ddiv_rn(det_exp64(dsub((double)fmul(key_value(S[r]), p.inv_temperature), ymax)), Z);
+    } else {
+      ids[r] = -1;
+      prs[r] = 0.0f;
+    }
+  }
+  a.n_surv[row] = cnt;
+}
+
+// Whole-vocabulary draw at temperature from the y-statistics (no filter on):
+// tile weights w_t = floor(a_t 2^-sh), sh = ceil(log2 n_tiles) + 1; tile by
+// the first uniform (first tile whose inclusive prefix of w exceeds
+// floor(u1 W)), token inside it by the second (first whose inclusive prefix
+// of q52(y - m_t) exceeds floor(u2 s_t)).  The warp re-reads that one tile.
+// Processors on a tile held in registers without a staging buffer: each
+// override is applied by the lane that owns its slot (rare path).
+template <int VW>
+__device__ __forceinline__ void process_tile_regs(const SampleArgs& a, const pm_row_params& p, int64_t row,
+                                                  int tile, TileIn& ti) {
+  const int lane = threadIdx.x & 31;
+  const int64_t start = (int64_t)tile * kTile;
+  for (int i = ti.bb; i < ti.be; ++i) {
+    const int e = (int)(a.bias_tok[i] - start);
+    if ((e % (32 * VW)) / VW != lane) continue;
+    const int sl = (e / (32 * VW)) * VW + e % VW;
+    const float b = a.bias_val[i];
+#pragma unroll
+    for (int q = 0; q < 32; ++q)
+      if (q == sl) ti.v[q] = fadd(ti.v[q], b);
+  }
+  const int32_t* otok = a.ovr_tok + row * (int64_t)a.ovr_cap;
+  const uint32_t* oinf = a.ovr_info + row * (int64_t)a.ovr_cap;
+  for (int i = ti.ob; i < ti.oe; ++i) {
+    const int e = (int)(otok[i] - start);
+    if ((e % (32 * VW)) / VW != lane) continue;
+    const int sl = (e / (32 * VW)) * VW + e % VW;
+    const uint32_t info = oinf[i];
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      if (q != sl) continue;
+      float x = ti.v[q];
+      if (info & 1u) x = x < 0.0f ? fmul(x, p.repetition_penalty) : __fdiv_rn(x, p.repetition_penalty);
+      if (info & 2u) x = fsub(x, p.presence_penalty);
+      const uint32_t cnt = info >> 8;
+      if (cnt) x = fsub(x, fmul(p.frequency_penalty, (float)cnt));
+      ti.v[q] = x;
+    }
+  }
+  if (a.mask) {
+#pragma unroll
+    for (int j = 0; j < 32 / VW; ++j) {
+      const uint32_t w = __shfl_sync(kFull, ti.mw, j * VW + (lane * VW) / 32);
+      const uint32_t bits = w >> ((lane * VW) & 31);
+#pragma unroll
+      for (int c = 0; c < VW; ++c)
+        if (!((bits >> c) & 1u)) ti.v[j * VW + c] = -INFINITY;
+    }
+  }
+}
+
+template <typename T>
+__device__ __noinline__ int warp_full_draw(const SampleArgs& a, const pm_row_params& p, int64_t row, float* x_out) {
+  constexpr int VW = Lay<T>::VW;
+  const int lane = threadIdx.x & 31;
+  const int nt = a.n_tiles;
+  const TileStat* st = a.staty + row * (int64_t)nt;
+  float my;
+  {
+    float m = -INFINITY;
+    for (int t = lane; t < nt; t += 32) m = fmaxf(m, ld_cg(&st[t].m));
+    my = warp_max(m);
+  }
+  *x_out = -INFINITY;
+  if (!(my > -INFINITY)) return 0;
+  int sh = 1;
+  while ((1 << (sh - 1)) < nt) ++sh;
+  const double scale = __longlong_as_double((long long)(1023 - sh) << 52);  // 2^-sh
+  uint64_t W = 0;
+  for (int t = lane; t < nt; t += 32) W += __double2ull_rz(dmul(tile_weight(st, t, my), scale));
+  W = warp_sum_u64(W);
+  const uint64_t t1 = scale_u53(row_u53(a, row, 0), W);
+  int tt = nt - 1;
+  uint64_t carry = 0;
+  for (int base = 0; base < nt; base += 32) {
+    const int t = base + lane;
+    const uint64_t w = t < nt ? __double2ull_rz(dmul(tile_weight(st, t, my), scale)) : 0ull;
+    const uint64_t incl = carry + warp_incl_scan_u64(w);
+    const unsigned hit = __ballot_sync(kFull, t < nt && incl > t1);
+    if (hit) { tt = base + __ffs(hit) - 1; break; }
+    carry = __shfl_sync(kFull, incl, 31);
+  }
+  const float mt = ld_cg(&st[tt].m);
+  const uint64_t t2 = scale_u53(row_u53(a, row, 1), ld_cg(&st[tt].s));
+  const int64_t start = (int64_t)tt * kTile;
+  TileIn ti;
+  load_tile<T>(a, row, tt, ti);
+  process_tile_regs<VW>(a, p, row, tt, ti);
+  uint64_t acc = 0;
+  int tok = (int)start;
+  float tx = -INFINITY;
+  for (int j = 0; j < 32 / VW; ++j) {
+    uint64_t q[VW];
+    uint64_t ls = 0;
+#pragma unroll
+    for (int c = 0; c < VW; ++c) {
+      const float x = ti.v[j * VW + c];
+      const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
+      q[c] = q52(fsub(y, mt));
+      ls += q[c];
+    }
+    const uint64_t incl = acc + warp_incl_scan_u64(ls);
+    const unsigned hit = __ballot_sync(kFull, incl > t2);
+    if (hit) {
+      const int src = __ffs(hit) - 1;
+      int found = -1;
+      float fx = -INFINITY;
+      if (lane == src) {
+        uint64_t run = incl - ls;
+#pragma unroll
+        for (int c = 0; c < VW; ++c) {
+          run += q[c];
+          if (found < 0 && run > t2) { found = c; fx = ti.v[j * VW + c]; }
+        }
+      }
+      found = __shfl_sync(kFull, found, src);
+      tx = __shfl_sync(kFull, fx, src);
+      tok = (int)(start + j * 32 * VW + src * VW + found);
+      break;
+    }
+    acc = __shfl_sync(kFull, incl, 31);
+  }
+  *x_out = tx;
+  return tok;
+}
+
+// Row merge by the warp that completed the row: gathers the parts' results
+// and draws the token.  Returns the token (-1 when flagged); *x_tok the
+// chosen token's processed logit, *lse the row log-sum-exp (NaN if unused).
+template <typename T, int KC, int CAP>
+__device__ __noinline__ int warp_row_merge(const SampleArgs& a, int64_t row, int n_parts, uint64_t* cbuf,
+                                           unsigned* hist, float* x_tok, float* lse_out, int* n_surv_out) {
+  const int lane = threadIdx.x & 31;
+  const pm_row_params p = row_params(a, row);
+  const int mode = row_mode(p);
+  float c = __int_as_float(0x7fc00000);
+  float mx;
+  if (needs_xstats(a, p, mode)) c = warp_combine(a.statx + row * a.n_tiles, a.n_tiles, &mx);
+  *lse_out = c;
+  *n_surv_out = 0;
+  int tok = 0;
+  *x_tok = -INFINITY;
+  if (mode == kGreedy) {
+    uint64_t bk = 0;
+    for (int i = lane; i < n_parts; i += 32) {
+      const uint64_t k = ld_cg(&a.best[row * a.max_parts + i]);
+      bk = k > bk ? k : bk;
+    }
+    bk = warp_max_u64(bk);
+    tok = (int)key_index(bk);
+    *x_tok = key_value(bk);
+  } else if (mode == kCand) {
+    const int K = (p.top_k > 0 && p.top_k < KC) ? p.top_k : KC;
+    Cand cd;
+    cand_reset(cd);
+    // Parts in groups of 32: the counts in one round of loads (lane i: part
+    // p0+i), then the group's keys in flattened order, eight independent
+    // loads per lane per round; a key's part is found by a binary search
+    // over the lanes' inclusive prefix counts.
+    bool trimmed_any = false;
+    for (int p0 = 0; p0 < n_parts; p0 += 32) {
+      const int part = p0 + lane;
+      const int raw = part < n_parts ? ld_cg(&a.cand_n[row * a.max_parts + part]) : 0;
+      const int n = raw & 0x3fffffff;
+      trimmed_any |= __any_sync(kFull, (raw >> 30) & 1) != 0;
+      const int incl = warp_incl_scan(n);
+      const int tot = __shfl_sync(kFull, incl, 31);
+      for (int f0 = 0; f0 < tot; f0 += 256) {
+        uint64_t keys[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int f = f0 + u * 32 + lane;
+          int q = 0;  // number of group parts whose inclusive prefix is <= f
+#pragma unroll
+          for (int st = 16; st > 0; st >>= 1) {
+            const int v = __shfl_sync(kFull, incl, (q + st - 1) & 31);
+            if (q + st - 1 < 32 && v <= f) q += st;
+          }
+          const int qi = q < 32 ? q : 31;
+          const int iq = __shfl_sync(kFull, incl, qi);
+          const int nq = __shfl_sync(kFull, n, qi);
+          keys[u] = 0ull;
+          if (f < tot) {
+            const uint64_t* src = a.cand + (row * a.max_parts + p0 + qi) * (int64_t)KC;
+            keys[u] = ld_cg(&src[f - (iq - nq)]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) cand_offer_key<CAP>(keys[u], cbuf, hist, cd, K);
+      }
+    }
+    if (cd.cnt > K) cand_compact<CAP>(cbuf, hist, cd, K);
+    warp_sort_desc(cbuf, cd.cnt);
+    int ns = 0;
+    tok = warp_filter_draw(a, p, row, cbuf, cd.cnt, !trimmed_any, c, &ns);
+    *n_surv_out = ns;
+    if (tok >= 0) {
+      for (int r = 0; r < cd.cnt; ++r)
+        if ((int)key_index(cbuf[r]) == tok) { *x_tok = key_value(cbuf[r]); break; }
+      if (a.surv_ids && lane == 0) write_survivors(a, p, row, cbuf, ns);
+    }
+  } else {
+    tok = warp_full_draw<T>(a, p, row, x_tok);
+  }
+  return tok;
+}
+
+}  // namespace pm

@@ -19,6 +19,7 @@ from .params import ProcessorSettings, SamplerSettings, pack_rows, validate
 
 _ws_lock = threading.Lock()
 _ws_cache: dict = {}
+_params_cache: dict = {}
 
 
 def workspace(nbytes: int, device: torch.device, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
@@ -67,6 +68,47 @@ class _Keep:
         return t
 
 
+def _params_for(dev: torch.device, sampler, processors, B: int, V: int):
+    """(device params tensor, flags_any, top_k_max, per_row), cached by settings."""
+    single = not isinstance(sampler, (list, tuple)) and not isinstance(processors, (list, tuple))
+    if single:
+        s = sampler if sampler is not None else SamplerSettings()
+        p = processors if processors is not None else ProcessorSettings()
+        key = (dev.index, V, s, p)
+        hit = _params_cache.get(key)
+        if hit is not None:
+            return hit
+        validate(s, p, V)
+        samplers, procs, per_row = [s], [p], False
+    else:
+        samplers = _as_list(sampler, B, SamplerSettings())
+        procs = _as_list(processors, B, ProcessorSettings())
+        per_row = len(set(samplers)) > 1 or len(set(procs)) > 1
+        key = (dev.index, V, tuple(samplers) if per_row else samplers[0], tuple(procs) if per_row else procs[0])
+        hit = _params_cache.get(key)
+        if hit is not None:
+            return hit
+        for s, p in zip(samplers, procs):
+            validate(s, p, V)
+        if len({p.logit_bias for p in procs}) > 1:
+            raise ValueError("logit_bias must be the same for every row of one call")
+        if not per_row:
+            samplers, procs = samplers[:1], procs[:1]
+    raw, flags_any, top_k_max = pack_rows(samplers, procs)
+    params = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(dev)
+    bias = None
+    lb = procs[0].logit_bias
+    if lb:
+        bias = (torch.tensor([t for t, _ in lb], dtype=torch.int32, device=dev),
+                torch.tensor([float(v) for _, v in lb], dtype=torch.float32, device=dev), len(lb))
+    hit = (params, flags_any, top_k_max, per_row, procs, bias)
+    with _ws_lock:
+        if len(_params_cache) > 256:
+            _params_cache.clear()
+        _params_cache[key] = hit
+    return hit
+
+
 def build_rows(logits: torch.Tensor, sampler, processors, history, history_len, mask, keep: _Keep,
                feed: Optional[torch.Tensor] = None, feed_group: int = 0) -> L.Rows:
     if logits.dim() != 2:
@@ -77,16 +119,7 @@ def build_rows(logits: torch.Tensor, sampler, processors, history, history_len, 
         logits = keep(logits.contiguous())
     B, V = logits.shape
     dev = logits.device
-    samplers = _as_list(sampler, B, SamplerSettings())
-    procs = _as_list(processors, B, ProcessorSettings())
-    for s, p in zip(samplers, procs):
-        validate(s, p, V)
-    if len({p.logit_bias for p in procs}) > 1:
-        raise ValueError("logit_bias must be the same for every row of one call")
-    per_row = len(set(samplers)) > 1 or len(set(procs)) > 1
-    raw, flags_any, top_k_max = pack_rows(samplers if per_row else samplers[:1],
-                                          procs if per_row else procs[:1])
-    params = keep(torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(dev, non_blocking=False))
+    params, flags_any, top_k_max, per_row, procs, bias = _params_for(dev, sampler, processors, B, V)
     r = L.Rows()
     r.logits = logits.data_ptr()
     r.dtype = _dtype_code(logits)
@@ -116,11 +149,8 @@ def build_rows(logits: torch.Tensor, sampler, processors, history, history_len, 
             dummy = keep(torch.zeros((B // feed_group, 1), dtype=torch.int32, device=dev))
             hl = keep(torch.zeros(B // feed_group, dtype=torch.int32, device=dev))
             r.hist, r.hist_len, r.hist_stride = dummy.data_ptr(), hl.data_ptr(), 1
-    lb = procs[0].logit_bias
-    if lb:
-        toks = keep(torch.tensor([t for t, _ in lb], dtype=torch.int32, device=dev))
-        vals = keep(torch.tensor([float(v) for _, v in lb], dtype=torch.float32, device=dev))
-        r.bias_tokens, r.bias_values, r.n_bias = toks.data_ptr(), vals.data_ptr(), len(lb)
+    if bias is not None:
+        r.bias_tokens, r.bias_values, r.n_bias = bias[0].data_ptr(), bias[1].data_ptr(), bias[2]
     if mask is not None:
         m = mask
         if m.dtype not in (torch.int32, torch.uint32):
@@ -159,7 +189,7 @@ def sample_rows(logits: torch.Tensor, sampler: Union[SamplerSettings, Sequence[S
                 history: Optional[torch.Tensor] = None, history_len=None, mask: Optional[torch.Tensor] = None,
                 seed: int = 0, offset: int = 0, row_base: int = 0, gumbel: Optional[torch.Tensor] = None,
                 uniform: Optional[torch.Tensor] = None, return_lse: bool = False,
-                return_logprob: bool = False, survivors: int = 0):
+                return_logprob: bool = False, survivors: int = 0, return_status: bool = False):
     """Processors + log-softmax + sampler for every row, one fused pass.
 
     Returns a dict with "tokens" [B] int32 (and "lse", "logprob",
@@ -198,7 +228,8 @@ def sample_rows(logits: torch.Tensor, sampler: Union[SamplerSettings, Sequence[S
     ws = workspace(nbytes, dev, stream)
     rc = lib.pm_sample_rows(C.byref(r), C.byref(nz), C.byref(out), ws.data_ptr(), ws.numel(), stream.cuda_stream)
     L.check(rc, "pm_sample_rows")
-    res["status"] = status_view(ws, r)
+    if return_status:
+        res["status"] = status_view(ws, r)
     return res
 
 

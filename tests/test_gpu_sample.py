@@ -56,7 +56,7 @@ def run_both(x, s, p=None, hist=None, hist_len=None, mask=None, bf16=None, seed=
         mask=None if mask is None else torch.from_numpy(mask.view(np.int32)).to(dev),
         gumbel=None if g is None else torch.from_numpy(g).to(dev),
         uniform=None if u is None else torch.from_numpy(u).to(dev), seed=1234, offset=7,
-        return_lse=want_lse, survivors=surv)
+        return_lse=want_lse, survivors=surv, return_status=True)
     torch.cuda.synchronize()
     got = {k: v.cpu().numpy() for k, v in res.items()}
     return ref, got
