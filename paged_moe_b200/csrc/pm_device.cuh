@@ -52,11 +52,75 @@ __device__ __forceinline__ float det_expf(float d) {
   return __int_as_float(__float_as_int(p) + (k << 23));
 }
 
-// floor(e^d * 2^52); d < -38, -inf or NaN -> 0 (e^-38 < 2^-52).
+// floor(e * 2^52) of a positive normal fp32 e below 2^7, from its bits:
+// e = mant * 2^(E - 150), so e * 2^52 = mant * 2^(E - 98), exactly.
+__device__ __forceinline__ uint64_t q52_from_bits(uint32_t be) {
+  const uint64_t mant = (uint64_t)((be & 0x7FFFFFu) | 0x800000u);
+  return (mant << 32) >> (130u - (be >> 23));
+}
+
+// floor(e^d * 2^52) with e^d = det_expf(d); 0 for d < -38, -inf or NaN.
+// Clamping d to -38 gives the same value as cutting there: det_expf(-38)
+// * 2^52 < 1.  Branch-free, and the conversion is an exact integer shift.
 __device__ __forceinline__ uint64_t q52(float d) {
-  if (!(d >= -38.0f)) return 0ull;
-  const float e = det_expf(d);
-  return __float2ull_rz(fmul(e, 0x1p52f));
+  d = fmaxf(d, -38.0f);  // NaN -> -38
+  const float t = fmul(d, 0x1.715476p+0f);
+  const float tm = fadd(t, 12582912.0f);
+  const float kf = fsub(tm, 12582912.0f);
+  float r = ffma(-kf, 0x1.62e4p-1f, d);
+  r = ffma(-kf, 0x1.7f7d1cp-20f, r);
+  float p = 0x1.a01a02p-13f;
+  p = ffma(p, r, 0x1.6c16c2p-10f);
+  p = ffma(p, r, 0x1.111112p-7f);
+  p = ffma(p, r, 0x1.555556p-5f);
+  p = ffma(p, r, 0x1.555556p-3f);
+  p = ffma(p, r, 0x1.0p-1f);
+  p = ffma(p, r, 1.0f);
+  p = ffma(p, r, 1.0f);
+  const int k = (int)(__float_as_uint(tm) - 0x4B400000u);  // tm = 1.5 * 2^23 + k exactly
+  return q52_from_bits(__float_as_uint(p) + ((uint32_t)k << 23));
+}
+
+// Packed pairs of fp32 (Blackwell f32x2 arithmetic): each half is an
+// independent IEEE fp32 operation with round-to-nearest.
+__device__ __forceinline__ uint64_t pk(float lo, float hi) {
+  return ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// q52 of two values at once; bit-identical to two q52 calls.
+__device__ __forceinline__ void q52x2(float d0, float d1, uint64_t& q0, uint64_t& q1) {
+  const uint64_t D = pk(fmaxf(d0, -38.0f), fmaxf(d1, -38.0f));
+  const uint64_t T = mul2(D, pk(0x1.715476p+0f, 0x1.715476p+0f));
+  const uint64_t TM = add2(T, pk(12582912.0f, 12582912.0f));
+  const uint64_t KF = add2(TM, pk(-12582912.0f, -12582912.0f));
+  uint64_t R = fma2(KF, pk(-0x1.62e4p-1f, -0x1.62e4p-1f), D);
+  R = fma2(KF, pk(-0x1.7f7d1cp-20f, -0x1.7f7d1cp-20f), R);
+  uint64_t P = pk(0x1.a01a02p-13f, 0x1.a01a02p-13f);
+  P = fma2(P, R, pk(0x1.6c16c2p-10f, 0x1.6c16c2p-10f));
+  P = fma2(P, R, pk(0x1.111112p-7f, 0x1.111112p-7f));
+  P = fma2(P, R, pk(0x1.555556p-5f, 0x1.555556p-5f));
+  P = fma2(P, R, pk(0x1.555556p-3f, 0x1.555556p-3f));
+  P = fma2(P, R, pk(0x1.0p-1f, 0x1.0p-1f));
+  P = fma2(P, R, pk(1.0f, 1.0f));
+  P = fma2(P, R, pk(1.0f, 1.0f));
+  const uint32_t k0 = (uint32_t)TM - 0x4B400000u, k1 = (uint32_t)(TM >> 32) - 0x4B400000u;
+  q0 = q52_from_bits((uint32_t)P + (k0 << 23));
+  q1 = q52_from_bits((uint32_t)(P >> 32) + (k1 << 23));
 }
 
 // e^d in fp64 for d <= ~0; d < -700 or NaN -> 0.

@@ -12,9 +12,9 @@
 //      sum of floor(e^(x - max) 2^52)) when the row needs them,
 //   4. feeds the row's candidate search: the greedy argmax, or a warp
 //      candidate buffer behind a running threshold for top-k style filters.
-// The CTA that finishes a row's last chunk (self-resetting atomicInc
-// counter, no spin-wait anywhere) merges the row: log-sum-exp from the tile
-// statistics, the row's top-K candidates, top-p / min-p, and the draw.
+// A second kernel, one warp per row, merges each row's parts: log-sum-exp
+// from the tile statistics, the row's top-K candidates, top-p / min-p, and
+// the draw.
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -41,6 +41,8 @@ struct PartState {
   float best_x;
   int best_e;
   Cand cd;
+  bool published;   // a compaction raised the threshold since the last publish
+  uint64_t rtau;    // the row's shared threshold, loaded one tile ahead
 };
 
 __device__ __forceinline__ void part_begin(const SampleArgs& a, int64_t row, int first_tile, int KC,
@@ -53,6 +55,24 @@ __device__ __forceinline__ void part_begin(const SampleArgs& a, int64_t row, int
   ps.best_x = -INFINITY;          // a part whose values are all -inf answers its first token
   ps.best_e = first_tile * kTile;
   cand_reset(ps.cd);
+  ps.published = false;
+  ps.rtau = 0;
+}
+
+// Share the part's threshold with the other parts of the row, and adopt
+// theirs: the K-th largest key a part holds is a lower bound for the row's
+// K-th largest key, so keys at or below the largest such bound can never be
+// selected.  Dropping them makes the part's list incomplete ("trimmed").
+__device__ __forceinline__ void share_threshold(const SampleArgs& a, int64_t row, PartState& ps) {
+  if (ps.published) {
+    if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<unsigned long long*>(&a.row_tau[row]), ps.cd.tau);
+    ps.published = false;
+  }
+  if (ps.rtau > ps.cd.tau) {
+    ps.cd.tau = ps.rtau;
+    ps.cd.tau_x = key_value(ps.rtau);
+    ps.cd.trimmed = true;
+  }
 }
 
 // Fill stage s of the warp's ring with tile gi by bulk copies (lane 0), when
@@ -109,7 +129,7 @@ __device__ __forceinline__ void scan_value(float x, int e, int start, float mref
     } else if constexpr (MODE == kGreedy) {
       if (x > ps.best_x) { ps.best_x = x; ps.best_e = start + e; }
     } else {
-      cand_offer_one<CAP>(x, (uint32_t)(start + e), wm->cand, wm->hist, ps.cd, ps.K);
+      if (cand_offer_one<CAP>(x, (uint32_t)(start + e), wm->cand, wm->hist, ps.cd, ps.K)) ps.published = true;
     }
   } else if constexpr (PASS == 2) {
     acc.sx += q52(fsub(x, mref));
@@ -131,9 +151,45 @@ __device__ __forceinline__ void scan_pass(const float* buf, bool dense, uint32_t
     for (int j = 0; j < 32 / VW; ++j) {
       float x[VW];
       read_step<S>(buf, j, lane, x);
+      if constexpr (PASS == 1) {
+        const int e0 = j * 32 * VW + lane * VW;
+        float lmax = x[0];
 #pragma unroll
-      for (int c = 0; c < VW; ++c)
-        scan_value<PASS, MODE, KC>(x[c], j * 32 * VW + lane * VW + c, start, mref, inv_t, ps, acc, wm);
+        for (int c = 1; c < VW; ++c) lmax = fmaxf(lmax, x[c]);
+        acc.mx = fmaxf(acc.mx, lmax);
+        if constexpr (MODE == kFullDraw) {
+#pragma unroll
+          for (int c = 0; c < VW; ++c)
+            if (x[c] > -INFINITY) acc.my = fmaxf(acc.my, fmul(x[c], inv_t));
+        } else if constexpr (MODE == kGreedy) {
+          if (lmax > ps.best_x) {
+#pragma unroll
+            for (int c = 0; c < VW; ++c)
+              if (x[c] > ps.best_x) { ps.best_x = x[c]; ps.best_e = start + e0 + c; }
+          }
+        } else {
+          if (cand_offer_vec<VW, StreamMem<KC>::CAP>(x, lmax, (uint32_t)(start + e0), wm->cand, wm->hist, ps.cd,
+                                                     ps.K))
+            ps.published = true;
+        }
+      } else {
+        // exact sums, two values per packed f32x2 evaluation
+#pragma unroll
+        for (int c = 0; c < VW; c += 2) {
+          float d0, d1;
+          if constexpr (PASS == 2) {
+            d0 = fsub(x[c], mref);
+            d1 = fsub(x[c + 1], mref);
+          } else {
+            d0 = fsub(x[c] > -INFINITY ? fmul(x[c], inv_t) : -INFINITY, mref);
+            d1 = fsub(x[c + 1] > -INFINITY ? fmul(x[c + 1], inv_t) : -INFINITY, mref);
+          }
+          uint64_t q0, q1;
+          q52x2(d0, d1, q0, q1);
+          if constexpr (PASS == 2) acc.sx += q0 + q1;
+          else acc.sy += q0 + q1;
+        }
+      }
     }
     return;
   }
@@ -152,6 +208,94 @@ __device__ __forceinline__ void scan_pass(const float* buf, bool dense, uint32_t
       x = read_elem<S>(buf, e);
     }
     scan_value<PASS, MODE, KC>(x, e, start, mref, inv_t, ps, acc, wm);
+  }
+}
+
+// Exact sums over n compacted fp32 values (two per packed evaluation).
+template <int PASS>
+__device__ __forceinline__ uint64_t sum_compacted(const float* buf, int n, float mref, float inv_t) {
+  const int lane = threadIdx.x & 31;
+  uint64_t sum = 0;
+  for (int i = 2 * lane; i < n; i += 64) {
+    float x0 = buf[i];
+    float x1 = i + 1 < n ? buf[i + 1] : -INFINITY;
+    if constexpr (PASS == 3) {
+      x0 = fmul(x0, inv_t);
+      x1 = x1 > -INFINITY ? fmul(x1, inv_t) : -INFINITY;
+    }
+    uint64_t q0, q1;
+    q52x2(fsub(x0, mref), fsub(x1, mref), q0, q1);
+    sum += q0 + q1;
+  }
+  return sum;
+}
+
+// A masked (or ragged) tile: one dense pass applies the per-slot allowed
+// bits, does the maxima and the selection, and compacts the allowed values
+// in place at the front of the buffer (their order is irrelevant to the
+// exact integer sums); the sums then run over the compacted values only.
+template <int MODE, int KC>
+__device__ __forceinline__ void scan_tile_masked(const SampleArgs& a, int64_t row, int tile, float* buf,
+                                                 uint32_t slots, PartState& ps, StreamMem<KC>* wm) {
+  constexpr int VW = 4;
+  const int lane = threadIdx.x & 31;
+  const int start = tile * kTile;
+  const float inv_t = ps.p.inv_temperature;
+  const bool compact = ps.needx || MODE == kFullDraw;
+  float mx = -INFINITY, my = -INFINITY;
+  int base = 0;
+#pragma unroll 2
+  for (int j = 0; j < 32 / VW; ++j) {
+    float x[VW];
+    read_step<float>(buf, j, lane, x);
+    const uint32_t bits = (slots >> (j * VW)) & ((1u << VW) - 1u);
+#pragma unroll
+    for (int c = 0; c < VW; ++c)
+      if (!((bits >> c) & 1u)) x[c] = -INFINITY;
+    const int e0 = j * 32 * VW + lane * VW;
+    float lmax = x[0];
+#pragma unroll
+    for (int c = 1; c < VW; ++c) lmax = fmaxf(lmax, x[c]);
+    mx = fmaxf(mx, lmax);
+    if constexpr (MODE == kFullDraw) {
+#pragma unroll
+      for (int c = 0; c < VW; ++c)
+        if (x[c] > -INFINITY) my = fmaxf(my, fmul(x[c], inv_t));
+    } else if constexpr (MODE == kGreedy) {
+      if (lmax > ps.best_x) {
+#pragma unroll
+        for (int c = 0; c < VW; ++c)
+          if (x[c] > ps.best_x) { ps.best_x = x[c]; ps.best_e = start + e0 + c; }
+      }
+    } else {
+      if (cand_offer_vec<VW, StreamMem<KC>::CAP>(x, lmax, (uint32_t)(start + e0), wm->cand, wm->hist, ps.cd, ps.K))
+        ps.published = true;
+    }
+    if (compact) {
+      const int nv = __popc(bits);
+      const int incl = warp_incl_scan(nv);
+      int pos = base + incl - nv;
+      __syncwarp();  // every lane has this step's values in registers
+#pragma unroll
+      for (int c = 0; c < VW; ++c)
+        if ((bits >> c) & 1u) buf[pos++] = x[c];
+      base += __shfl_sync(kFull, incl, 31);
+    }
+  }
+  __syncwarp();
+  if (ps.needx) {
+    const float m = warp_max(mx);
+    uint64_t sum = 0;
+    if (m > -INFINITY) sum = sum_compacted<2>(buf, base, m, inv_t);
+    sum = warp_sum_u64(sum);
+    if (lane == 0) { TileStat t; t.m = m; t.pad = 0; t.s = sum; a.statx[row * a.n_tiles + tile] = t; }
+  }
+  if constexpr (MODE == kFullDraw) {
+    const float m = warp_max(my);
+    uint64_t sum = 0;
+    if (m > -INFINITY) sum = sum_compacted<3>(buf, base, m, inv_t);
+    sum = warp_sum_u64(sum);
+    if (lane == 0) { TileStat t; t.m = m; t.pad = 0; t.s = sum; a.staty[row * a.n_tiles + tile] = t; }
   }
 }
 
@@ -184,15 +328,21 @@ __device__ __forceinline__ void scan_tile_mode(const SampleArgs& a, int64_t row,
 
 // Statistics and candidate search of one staged tile, values of type S in buf.
 template <typename S, int KC>
-__device__ __forceinline__ void scan_tile(const SampleArgs& a, int64_t row, int tile, const float* buf,
+__device__ __forceinline__ void scan_tile(const SampleArgs& a, int64_t row, int tile, float* buf,
                                           const uint32_t* mw, PartState& ps, StreamMem<KC>* wm) {
-  constexpr int VW = Vec<S>::VW;
   const int lane = threadIdx.x & 31;
   const int n_valid = tile_valid(a, tile);
   const bool masked = a.mask != nullptr;
-  const bool dense = !masked && n_valid == kTile;
-  uint32_t slots = 0xffffffffu;
-  if (masked) slots = slot_mask<VW>(mw);
+  if (!masked && n_valid == kTile) {
+    if (ps.mode == kGreedy) scan_tile_mode<S, kGreedy, KC>(a, row, tile, buf, true, ~0u, ps, wm);
+    else if (ps.mode == kCand) scan_tile_mode<S, kCand, KC>(a, row, tile, buf, true, ~0u, ps, wm);
+    else scan_tile_mode<S, kFullDraw, KC>(a, row, tile, buf, true, ~0u, ps, wm);
+    return;
+  }
+  // masked or ragged: fp32 slots (a bf16 tile is widened in place first)
+  if constexpr (sizeof(S) == 2) expand_bf16_in_place(buf);
+  constexpr int VW = 4;
+  uint32_t slots = masked ? slot_mask<VW>(mw) : 0xffffffffu;
   if (n_valid < kTile) {
     uint32_t keep = 0;
 #pragma unroll
@@ -200,22 +350,29 @@ __device__ __forceinline__ void scan_tile(const SampleArgs& a, int64_t row, int 
       if (slot_to_elem<VW>(sl, lane) < n_valid) keep |= 1u << sl;
     slots &= keep;
   }
-  if (ps.mode == kGreedy) scan_tile_mode<S, kGreedy, KC>(a, row, tile, buf, dense, slots, ps, wm);
-  else if (ps.mode == kCand) scan_tile_mode<S, kCand, KC>(a, row, tile, buf, dense, slots, ps, wm);
-  else scan_tile_mode<S, kFullDraw, KC>(a, row, tile, buf, dense, slots, ps, wm);
+  int busiest = __popc(slots);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) busiest = max(busiest, __shfl_xor_sync(kFull, busiest, o));
+  if (busiest <= 12) {
+    // few allowed values: visit them slot by slot
+    if (ps.mode == kGreedy) scan_tile_mode<float, kGreedy, KC>(a, row, tile, buf, false, slots, ps, wm);
+    else if (ps.mode == kCand) scan_tile_mode<float, kCand, KC>(a, row, tile, buf, false, slots, ps, wm);
+    else scan_tile_mode<float, kFullDraw, KC>(a, row, tile, buf, false, slots, ps, wm);
+    return;
+  }
+  if (ps.mode == kGreedy) scan_tile_masked<kGreedy, KC>(a, row, tile, buf, slots, ps, wm);
+  else if (ps.mode == kCand) scan_tile_masked<kCand, KC>(a, row, tile, buf, slots, ps, wm);
+  else scan_tile_masked<kFullDraw, KC>(a, row, tile, buf, slots, ps, wm);
 }
 
-// End of a row part: publish it; the warp that completes the row merges it.
+// End of a row part: publish its candidates (or its argmax) for the merge.
 template <typename T, int KC>
 __device__ __forceinline__ void part_end(const SampleArgs& a, int64_t row, int64_t gw, PartState& ps,
                                          StreamMem<KC>* wm) {
   constexpr int CAP = StreamMem<KC>::CAP;
   const int lane = threadIdx.x & 31;
   const int64_t total = a.rows * a.n_tiles;
-  const int64_t w0 = owner_warp(row * a.n_tiles, total, a.n_warps);
-  const int64_t w1 = owner_warp((row + 1) * a.n_tiles - 1, total, a.n_warps);
-  const int part = (int)(gw - w0);
-  const int n_parts = (int)(w1 - w0 + 1);
+  const int part = (int)(gw - owner_warp(row * a.n_tiles, total, a.n_warps));
   if (ps.mode == kGreedy) {
     const uint64_t k = rankkey(ps.best_x, (uint32_t)ps.best_e);
     const uint64_t wk = warp_max_u64(k);
@@ -226,26 +383,49 @@ __device__ __forceinline__ void part_end(const SampleArgs& a, int64_t row, int64
     for (int i = lane; i < ps.cd.cnt; i += 32) dst[i] = wm->cand[i];
     if (lane == 0) a.cand_n[row * a.max_parts + part] = ps.cd.cnt | (ps.cd.trimmed ? (1 << 30) : 0);
   }
-  __threadfence();
   __syncwarp();
-  unsigned prev = 0;
-  if (lane == 0) prev = atomicInc(&a.row_done[row], (unsigned)(n_parts - 1));
-  prev = __shfl_sync(kFull, prev, 0);
-  if (prev != (unsigned)(n_parts - 1)) return;
-  __threadfence();
-  float x_tok, lse;
-  int ns;
-  const int tok = warp_row_merge<T, KC, CAP>(a, row, n_parts, wm->cand, wm->hist, &x_tok, &lse, &ns);
-  if (lane == 0) {
-    const int32_t prevs = a.prep_ran ? ld_cg(&a.status[row]) : 0;
-    a.status[row] = prevs | (tok < 0 ? 1 : 0);
-    a.tokens[row] = tok;
-    if (a.lse_out) a.lse_out[row] = lse;
-    if (a.row_lse) a.row_lse[row] = lse;
-    if (a.tok_logprob) a.tok_logprob[row] = tok >= 0 ? fsub(x_tok, lse) : __int_as_float(0x7fc00000);
-    if (a.n_surv && (ps.mode != kCand || !a.surv_ids)) a.n_surv[row] = ps.mode == kCand ? ns : 0;
+}
+
+// Row outputs (lane 0).
+__device__ __forceinline__ void write_row(const SampleArgs& a, int64_t row, int mode, int tok, float x_tok,
+                                          float lse, int ns) {
+  const int32_t prevs = a.prep_ran ? ld_cg(&a.status[row]) : 0;
+  a.status[row] = prevs | (tok < 0 ? 1 : 0);
+  a.tokens[row] = tok;
+  if (a.lse_out) a.lse_out[row] = lse;
+  if (a.row_lse) a.row_lse[row] = lse;
+  if (a.tok_logprob) a.tok_logprob[row] = tok >= 0 ? fsub(x_tok, lse) : __int_as_float(0x7fc00000);
+  if (a.n_surv && (mode != kCand || !a.surv_ids)) a.n_surv[row] = mode == kCand ? ns : 0;
+}
+
+// Merge of every row's parts: one warp per row.  Launched after the
+// streaming kernel on the same stream (programmatic dependent launch: it may
+// start while the streaming kernel drains, and waits for its results).
+template <typename T, int KC>
+__global__ void __launch_bounds__(256) k_row_merge(const __grid_constant__ SampleArgs a) {
+  constexpr int CAP = StreamMem<KC>::CAP;
+  struct MergeMem {
+    uint64_t cand[CAP];
+    unsigned hist[256];
+  };
+  extern __shared__ __align__(128) unsigned char smem_merge[];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  MergeMem* mm = reinterpret_cast<MergeMem*>(smem_merge) + wid;
+  const int64_t total = a.rows * a.n_tiles;
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + wid; row < a.rows;
+       row += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    const int n_parts = (int)(owner_warp((row + 1) * a.n_tiles - 1, total, a.n_warps) -
+                              owner_warp(row * a.n_tiles, total, a.n_warps) + 1);
+    float x_tok, lse;
+    int ns;
+    const int tok = warp_row_merge<T, KC, CAP>(a, row, n_parts, mm->cand, mm->hist, &x_tok, &lse, &ns);
+    if (lane == 0) {
+      write_row(a, row, row_mode(row_params(a, row)), tok, x_tok, lse, ns);
+      a.row_tau[row] = 0;  // ready for the next call
+    }
+    __syncwarp();
   }
-  __syncwarp();
 }
 
 // The streaming kernel.  Warp gw owns the flattened tiles
@@ -256,11 +436,12 @@ __device__ __forceinline__ void part_end(const SampleArgs& a, int64_t row, int64
 // wait for one another; the only waits are the bounded mbarrier waits on the
 // warp's own copies.
 template <typename T, int KC>
-__global__ void __launch_bounds__(kThreadsS) k_sample_stream(const __grid_constant__ SampleArgs a) {
+__global__ void __launch_bounds__(kThreadsS, 3) k_sample_stream(const __grid_constant__ SampleArgs a) {
   using SMem = StreamMem<KC>;
   extern __shared__ __align__(128) unsigned char smem_stream[];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   SMem* wm = reinterpret_cast<SMem*>(smem_stream) + wid;
+  asm volatile("griddepcontrol.launch_dependents;");
   const int64_t total = a.rows * a.n_tiles;
   const int64_t gw = (int64_t)blockIdx.x * kWarpsS + wid;
   if (gw >= a.n_warps) return;
@@ -309,6 +490,7 @@ __global__ void __launch_bounds__(kThreadsS) k_sample_stream(const __grid_consta
       oe = off[1];
     }
     if (a.bias_off) { bb = a.bias_off[tile]; be = a.bias_off[tile + 1]; }
+    if (ps.mode == kCand) share_threshold(a, row, ps);
     if (oe > ob || be > bb) {
       if constexpr (sizeof(T) == 2) expand_bf16_in_place(buf);
       apply_overrides_smem(a, ps.p, row, tile, ob, oe, bb, be, buf);
@@ -316,6 +498,7 @@ __global__ void __launch_bounds__(kThreadsS) k_sample_stream(const __grid_consta
     } else {
       scan_tile<T, KC>(a, row, tile, buf, wm->mask[s], ps, wm);
     }
+    if (ps.mode == kCand) ps.rtau = ld_cg(&a.row_tau[row]);  // for the next tile, in flight meanwhile
     __syncwarp();
     armed &= ~(1u << s);
     if (gi + kStages < g1) {
@@ -468,7 +651,7 @@ int occupancy_for(int dtype, int KC) {
 struct Layout {
   int n_tiles = 0, KC = 0, ovr_cap = 0, max_parts = 0;
   int64_t n_warps = 0;
-  size_t row_done = 0, status = 0, statx = 0, staty = 0, cand = 0, cand_n = 0, best = 0, ovr_tok = 0,
+  size_t row_done = 0, row_tau = 0, status = 0, statx = 0, staty = 0, cand = 0, cand_n = 0, best = 0, ovr_tok = 0,
          ovr_info = 0, ovr_off = 0, bias_off = 0, row_lse = 0, total = 0;
 };
 
@@ -505,6 +688,7 @@ int plan(const pm_rows* r, Layout* L) {
   auto take = [&](size_t bytes) { o = align_up(o, 256); const size_t at = o; o += bytes; return at; };
   L->row_done = take(sizeof(uint32_t) * R);
   L->status = take(sizeof(int32_t) * R);
+  L->row_tau = take(sizeof(uint64_t) * R);
   L->statx = take(sizeof(pm::TileStat) * R * L->n_tiles);
   L->staty = take(sizeof(pm::TileStat) * R * L->n_tiles);
   L->cand = take(sizeof(uint64_t) * R * L->max_parts * L->KC);
@@ -552,6 +736,7 @@ int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::Sample
   a.cand_n = reinterpret_cast<int32_t*>(ws + L.cand_n);
   a.best = reinterpret_cast<uint64_t*>(ws + L.best);
   a.row_done = reinterpret_cast<uint32_t*>(ws + L.row_done);
+  a.row_tau = reinterpret_cast<uint64_t*>(ws + L.row_tau);
   a.status = reinterpret_cast<int32_t*>(ws + L.status);
   a.row_lse = reinterpret_cast<float*>(ws + L.row_lse);
   a.ovr_tok = nullptr;
@@ -614,7 +799,34 @@ int launch_stream(const pm::SampleArgs& a, cudaStream_t st) {
   const int64_t grid = (a.n_warps + pm::kWarpsS - 1) / pm::kWarpsS;
   if (grid == 0) return PM_OK;
   pm::k_sample_stream<T, KC><<<(unsigned)grid, pm::kThreadsS, smem, st>>>(a);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  // the row merges: one warp per row, chained by programmatic dependent launch
+  constexpr int kMergeWarps = 8;
+  const size_t msmem = (sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * kMergeWarps;
+  static std::once_flag once;
+  std::call_once(once, [msmem] {
+    cudaFuncSetAttribute(pm::k_row_merge<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem);
+  });
+  int64_t mgrid = (a.rows + kMergeWarps - 1) / kMergeWarps;
+  const int64_t mcap = (int64_t)num_sms() * 8;
+  if (mgrid > mcap) mgrid = mcap;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)mgrid);
+  cfg.blockDim = dim3(32 * kMergeWarps);
+  cfg.dynamicSmemBytes = msmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, pm::k_row_merge<T, KC>, a);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // no programmatic launch here: plain stream order
+    pm::k_row_merge<T, KC><<<(unsigned)mgrid, 32 * kMergeWarps, msmem, st>>>(a);
+    e = cudaGetLastError();
+  }
   return e == cudaSuccess ? PM_OK : cuda_fail(e);
 }
 

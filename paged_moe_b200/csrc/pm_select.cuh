@@ -48,16 +48,30 @@ __device__ __forceinline__ int warp_find_digit(const unsigned* hist, int need, i
 template <int MAXPER>
 __device__ uint64_t warp_select_topk(uint64_t* buf, int cnt, int K, unsigned* hist) {
   const int lane = threadIdx.x & 31;
-  uint64_t prefix = 0;
+  // Skip the leading bits every key shares: the first digit starts at the
+  // highest bit where the smallest and largest key differ, so the first
+  // histogram spreads over the bins instead of piling into one.
+  uint64_t kmin = ~0ull, kmax = 0ull;
+  for (int i = lane; i < cnt; i += 32) {
+    const uint64_t k = buf[i];
+    kmin = k < kmin ? k : kmin;
+    kmax = k > kmax ? k : kmax;
+  }
+  kmin = warp_min_u64(kmin);
+  kmax = warp_max_u64(kmax);
+  // bits at and above `hi` are common to every key still in play
+  int hi = 64 - __clzll(kmin ^ kmax);  // keys are unique, so kmin != kmax
+  uint64_t prefix = hi >= 64 ? 0ull : (kmax >> hi) << hi;
   int need = K;
-  int shift = 56;
   for (;;) {
+    const int w = hi < 8 ? hi : 8;
+    const int shift = hi - w;
     for (int i = lane; i < 256; i += 32) hist[i] = 0;
     __syncwarp();
     for (int i = lane; i < cnt; i += 32) {
       const uint64_t k = buf[i];
-      const bool match = (shift == 56) || (((k ^ prefix) >> (shift + 8)) == 0);
-      if (match) atomicAdd(&hist[(k >> shift) & 255], 1u);
+      const bool match = hi >= 64 || ((k ^ prefix) >> hi) == 0;
+      if (match) atomicAdd(&hist[(k >> shift) & ((1u << w) - 1u)], 1u);
     }
     __syncwarp();
     int above, in_bin;
@@ -66,7 +80,7 @@ __device__ uint64_t warp_select_topk(uint64_t* buf, int cnt, int K, unsigned* hi
     need -= above;
     prefix |= (uint64_t)d << shift;
     if (in_bin == need || shift == 0) break;
-    shift -= 8;
+    hi = shift;
   }
   // keep keys >= prefix (low bits of prefix below `shift` are zero)
   uint64_t mine[MAXPER];
@@ -76,7 +90,7 @@ __device__ uint64_t warp_select_topk(uint64_t* buf, int cnt, int K, unsigned* hi
     mine[r] = (i < cnt) ? buf[i] : 0ull;
   }
   __syncwarp();
-  uint64_t kmin = ~0ull;
+  uint64_t kept_min = ~0ull;
   int base = 0;
 #pragma unroll
   for (int r = 0; r < MAXPER; ++r) {
@@ -84,12 +98,12 @@ __device__ uint64_t warp_select_topk(uint64_t* buf, int cnt, int K, unsigned* hi
     const unsigned bal = __ballot_sync(kFull, keep);
     if (keep) {
       buf[base + __popc(bal & ((1u << lane) - 1u))] = mine[r];
-      kmin = mine[r] < kmin ? mine[r] : kmin;
+      kept_min = mine[r] < kept_min ? mine[r] : kept_min;
     }
     base += __popc(bal);
   }
   __syncwarp();
-  return warp_min_u64(kmin);
+  return warp_min_u64(kept_min);
 }
 
 // Block-level: the K largest of U[0..n) sorted descending into S[0..m),

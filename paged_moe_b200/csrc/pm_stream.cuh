@@ -22,7 +22,7 @@ constexpr int kStages = 3;
 // Per-warp shared memory of the streaming kernels.
 template <int KC>
 struct alignas(128) StreamMem {
-  static constexpr int CAP = KC + 128;  // KC kept + one push round of 4 values per lane
+  static constexpr int CAP = KC + 384;  // KC kept + room for several push rounds between compactions
   float tile[kStages][kTile];           // fp32 tile, or a bf16 tile in the first half
   uint32_t mask[kStages][32];
   uint64_t bar[kStages];

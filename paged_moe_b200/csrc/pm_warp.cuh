@@ -40,21 +40,53 @@ __device__ __forceinline__ void cand_compact(uint64_t* buf, unsigned* hist, Cand
   c.trimmed = true;
 }
 
+// Offer VW consecutive values per lane (tokens tok0 .. tok0+VW-1; lmax their
+// maximum) to the buffer.  One vote per group in the common case.
+template <int VW, int CAP>
+__device__ __forceinline__ bool cand_offer_vec(const float (&x)[VW], float lmax, uint32_t tok0, uint64_t* buf,
+                                               unsigned* hist, Cand& c, int K) {
+  const int lane = threadIdx.x & 31;
+  if (!__any_sync(kFull, lmax > -INFINITY && lmax >= c.tau_x)) return false;
+  unsigned valid = 0;
+#pragma unroll
+  for (int i = 0; i < VW; ++i)
+    if (x[i] > -INFINITY && x[i] >= c.tau_x && rankkey(x[i], tok0 + i) > c.tau) valid |= 1u << i;
+  const int nv = __popc(valid);
+  const int incl = warp_incl_scan(nv);
+  int pos = c.cnt + incl - nv;
+#pragma unroll
+  for (int i = 0; i < VW; ++i)
+    if ((valid >> i) & 1u) buf[pos++] = rankkey(x[i], tok0 + i);
+  c.cnt += __shfl_sync(kFull, incl, 31);
+  __syncwarp();
+  // the first compaction comes early (2K keys) to set a useful threshold
+  if (c.cnt > (c.trimmed ? CAP - 32 * VW : min(CAP - 32 * VW, 2 * K))) {
+    cand_compact<CAP>(buf, hist, c, K);
+    return true;
+  }
+  (void)lane;
+  return false;
+}
+
 // Offer one value per lane (token tok) to the buffer: appended when its key
 // beats the threshold.  The common case costs one compare and one vote.
 template <int CAP>
-__device__ __forceinline__ void cand_offer_one(float x, uint32_t tok, uint64_t* buf, unsigned* hist, Cand& c,
+__device__ __forceinline__ bool cand_offer_one(float x, uint32_t tok, uint64_t* buf, unsigned* hist, Cand& c,
                                                int K) {
   const int lane = threadIdx.x & 31;
   const bool pre = x > -INFINITY && x >= c.tau_x;
-  if (!__any_sync(kFull, pre)) return;
+  if (!__any_sync(kFull, pre)) return false;
   const uint64_t key = rankkey(x, tok);
   const bool ok = pre && key > c.tau;
   const unsigned bal = __ballot_sync(kFull, ok);
   if (ok) buf[c.cnt + __popc(bal & ((1u << lane) - 1u))] = key;
   c.cnt += __popc(bal);
   __syncwarp();
-  if (c.cnt > CAP - 32) cand_compact<CAP>(buf, hist, c, K);
+  if (c.cnt > CAP - 32) {
+    cand_compact<CAP>(buf, hist, c, K);
+    return true;
+  }
+  return false;
 }
 
 // Offer one key per lane (0 = nothing).
