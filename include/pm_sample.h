@@ -164,6 +164,35 @@ PM_API int pm_apply_processors(const pm_rows *rows, float *out, int64_t out_stri
 PM_API int pm_logprobs(const pm_rows *rows, float *out, int64_t out_stride, float *lse_out, void *workspace,
                 size_t workspace_bytes, void *stream);
 
+/* Draft acceptance of a verify pass.  rows->rows = requests * (k + 1): row
+ * i of request b holds the target logits that judge drafts[b, i] (i < k) or
+ * give the bonus token (i = k); rows->feed must be [y] + drafts per request
+ * (feed_group = k + 1) so each row's processors see history + [y] + drafts[:i]
+ * (reference verify_decode.py:889-898). */
+#define PM_VERIFY_MATCH 0     /* reference rule: sample every row, keep drafts while equal
+                                 (lookup_decode.py:363-369, verify_decode.py:915-921) */
+#define PM_VERIFY_RESIDUAL 1  /* speculative rejection sampling: accept draft i when
+                                 u_i * q_i(d) < p_i(d), else draw from max(p_i - q_i, 0) */
+
+typedef struct pm_verify_args {
+    int32_t mode;                /* PM_VERIFY_* */
+    const int32_t *drafts;       /* [requests, n_draft] */
+    int32_t n_draft;             /* k >= 0 */
+    const void *draft_logits;    /* residual: [requests * k, draft_row_stride] logits of q */
+    int32_t draft_dtype;         /* PM_DTYPE_* */
+    int64_t draft_row_stride;
+    const double *u_accept;      /* injected: [requests, k] uniforms, else Philox */
+    const double *u_residual;    /* injected: [requests] uniforms, else Philox */
+    int32_t *tokens;             /* out [requests, k + 1]: accepted drafts, then the
+                                    request's own token; -1 after it */
+    int32_t *n_accepted;         /* out [requests] */
+    int32_t *row_tokens;         /* optional out [requests * (k + 1)]: each row's sample */
+} pm_verify_args;
+
+PM_API size_t pm_verify_workspace_bytes(const pm_rows *rows, const pm_verify_args *v);
+PM_API int pm_verify(const pm_rows *rows, const pm_noise *noise, const pm_verify_args *v, void *workspace,
+                     size_t workspace_bytes, void *stream);
+
 /* Last CUDA error seen by this thread (cudaError_t value), 0 if none. */
 PM_API int pm_last_cuda_error(void);
 

@@ -17,11 +17,7 @@ _lib.load()
 
 from .engine import apply_processors, logprobs, sample_rows  # noqa: E402,F401
 from .sample_utils import make_logits_processors, make_sampler  # noqa: E402,F401
-
-try:  # verify / sharding live in their own modules
-    from .verify import verify  # noqa: E402,F401
-except ImportError:  # pragma: no cover - during bring-up only
-    pass
+from .verify import verify  # noqa: E402,F401
 
 __version__ = "0.1.0"
 

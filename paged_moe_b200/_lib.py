@@ -108,7 +108,7 @@ SIGNATURES = {
     "pm_apply_processors": (C.c_int, [_P, _P, C.c_int64, _P, C.c_size_t, _P]),
     "pm_logprobs": (C.c_int, [_P, _P, C.c_int64, _P, _P, C.c_size_t, _P]),
     "pm_verify_workspace_bytes": (C.c_size_t, [_P, _P]),
-    "pm_verify": (C.c_int, [_P, _P, _P, _P, _P, C.c_size_t, _P]),
+    "pm_verify": (C.c_int, [_P, _P, _P, _P, C.c_size_t, _P]),
     "pm_shard_summary_bytes": (C.c_size_t, [_P, _P]),
     "pm_shard_summarize": (C.c_int, [_P, _P, _P, _P, C.c_size_t, _P]),
     "pm_shard_merge": (C.c_int, [_P, _P, _P, _P, _P, _P, C.c_size_t, _P]),

@@ -420,10 +420,7 @@ __global__ void __launch_bounds__(256) k_row_merge(const __grid_constant__ Sampl
     float x_tok, lse;
     int ns;
     const int tok = warp_row_merge<T, KC, CAP>(a, row, n_parts, mm->cand, mm->hist, &x_tok, &lse, &ns);
-    if (lane == 0) {
-      write_row(a, row, row_mode(row_params(a, row)), tok, x_tok, lse, ns);
-      a.row_tau[row] = 0;  // ready for the next call
-    }
+    if (lane == 0) write_row(a, row, row_mode(row_params(a, row)), tok, x_tok, lse, ns);
     __syncwarp();
   }
 }
@@ -588,6 +585,8 @@ __global__ void k_bias_offsets(const int32_t* tok, int n, int n_tiles, int32_t* 
 
 }  // namespace pm
 
+#include "pm_verify_impl.cuh"
+
 // ============================================================================
 // host side
 // ============================================================================
@@ -651,7 +650,7 @@ int occupancy_for(int dtype, int KC) {
 struct Layout {
   int n_tiles = 0, KC = 0, ovr_cap = 0, max_parts = 0;
   int64_t n_warps = 0;
-  size_t row_done = 0, row_tau = 0, status = 0, statx = 0, staty = 0, cand = 0, cand_n = 0, best = 0, ovr_tok = 0,
+  size_t row_tau = 0, status = 0, statx = 0, staty = 0, cand = 0, cand_n = 0, best = 0, ovr_tok = 0,
          ovr_info = 0, ovr_off = 0, bias_off = 0, row_lse = 0, total = 0;
 };
 
@@ -659,7 +658,7 @@ int64_t owner(int64_t g, int64_t T, int64_t W) { return ((g + 1) * W + T - 1) / 
 
 int plan(const pm_rows* r, Layout* L) {
   if (!r || r->rows < 0 || r->vocab <= 0 || r->row_stride < r->vocab) return PM_ERR_ARG;
-  if (r->vocab > (int64_t)1024 * pm::kTile) return PM_ERR_UNSUPPORTED;  // 1024 tiles per row at most
+  if (r->vocab > (int64_t)32 * pm::kMaxPer * pm::kTile) return PM_ERR_UNSUPPORTED;  // 256 tiles per row at most
   L->n_tiles = (int)((r->vocab + pm::kTile - 1) / pm::kTile);
   int need = r->top_k_max > 0 ? r->top_k_max : 0;
   if (r->flags_any & PM_F_UNBOUNDED) need = need > 256 ? need : 256;
@@ -686,7 +685,6 @@ int plan(const pm_rows* r, Layout* L) {
   const int64_t R = r->rows;
   size_t o = 0;
   auto take = [&](size_t bytes) { o = align_up(o, 256); const size_t at = o; o += bytes; return at; };
-  L->row_done = take(sizeof(uint32_t) * R);
   L->status = take(sizeof(int32_t) * R);
   L->row_tau = take(sizeof(uint64_t) * R);
   L->statx = take(sizeof(pm::TileStat) * R * L->n_tiles);
@@ -735,7 +733,6 @@ int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::Sample
   a.cand = reinterpret_cast<uint64_t*>(ws + L.cand);
   a.cand_n = reinterpret_cast<int32_t*>(ws + L.cand_n);
   a.best = reinterpret_cast<uint64_t*>(ws + L.best);
-  a.row_done = reinterpret_cast<uint32_t*>(ws + L.row_done);
   a.row_tau = reinterpret_cast<uint64_t*>(ws + L.row_tau);
   a.status = reinterpret_cast<int32_t*>(ws + L.status);
   a.row_lse = reinterpret_cast<float*>(ws + L.row_lse);
@@ -792,14 +789,23 @@ int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::Sample
   return PM_OK;
 }
 
+bool has_cand_rows(const pm_rows* r) {
+  return r->top_k_max > 0 || (r->flags_any & (PM_F_TOP_P | PM_F_MIN_P));
+}
+
 template <typename T, int KC>
-int launch_stream(const pm::SampleArgs& a, cudaStream_t st) {
+int launch_stream(const pm::SampleArgs& a, bool cand_rows, cudaStream_t st) {
   stream_occupancy<T, KC>();
   const size_t smem = sizeof(pm::StreamMem<KC>) * pm::kWarpsS;
   const int64_t grid = (a.n_warps + pm::kWarpsS - 1) / pm::kWarpsS;
   if (grid == 0) return PM_OK;
+  cudaError_t e;
+  if (cand_rows) {  // the shared row thresholds start at zero ("nothing proven")
+    e = cudaMemsetAsync(a.row_tau, 0, sizeof(uint64_t) * a.rows, st);
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
   pm::k_sample_stream<T, KC><<<(unsigned)grid, pm::kThreadsS, smem, st>>>(a);
-  cudaError_t e = cudaGetLastError();
+  e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   // the row merges: one warp per row, chained by programmatic dependent launch
   constexpr int kMergeWarps = 8;
@@ -830,10 +836,106 @@ int launch_stream(const pm::SampleArgs& a, cudaStream_t st) {
   return e == cudaSuccess ? PM_OK : cuda_fail(e);
 }
 
-int launch_stream_any(int dtype, int KC, const pm::SampleArgs& a, cudaStream_t st) {
+int launch_stream_any(int dtype, int KC, const pm::SampleArgs& a, bool cand_rows, cudaStream_t st) {
   const bool bf = dtype == PM_DTYPE_BF16;
-  if (KC == 64) return bf ? launch_stream<__nv_bfloat16, 64>(a, st) : launch_stream<float, 64>(a, st);
-  return bf ? launch_stream<__nv_bfloat16, 256>(a, st) : launch_stream<float, 256>(a, st);
+  if (KC == 64) return bf ? launch_stream<__nv_bfloat16, 64>(a, cand_rows, st) : launch_stream<float, 64>(a, cand_rows, st);
+  return bf ? launch_stream<__nv_bfloat16, 256>(a, cand_rows, st) : launch_stream<float, 256>(a, cand_rows, st);
+}
+
+int check_noise(const pm_rows* rows, const pm_noise* noise) {
+  if (!noise) return PM_ERR_ARG;
+  if (noise->mode != PM_NOISE_PHILOX && noise->mode != PM_NOISE_INJECTED) return PM_ERR_ARG;
+  if (noise->mode == PM_NOISE_INJECTED) {
+    if (has_cand_rows(rows) && (!noise->gumbel || noise->gumbel_stride < rows->vocab)) return PM_ERR_ARG;
+    if ((rows->flags_any & PM_F_FULL) && !noise->uniform) return PM_ERR_ARG;
+  }
+  return PM_OK;
+}
+
+void set_noise(const pm_noise* noise, pm::SampleArgs& a) {
+  a.noise_mode = noise->mode;
+  a.seed = noise->seed;
+  a.offset = noise->offset;
+  a.row_base = noise->row_base;
+  a.gumbel = noise->gumbel;
+  a.gumbel_stride = noise->gumbel_stride;
+  a.uniform = noise->uniform;
+}
+
+// Workspace of a verify call: the sampling layout of the target rows, then
+// each row's sample and survivors, the pending residual rows, and the draft
+// rows' tile statistics and log-sum-exp.
+struct VLayout {
+  Layout L;
+  int k = 0, scap = 0;
+  int64_t B = 0, D = 0;
+  size_t rtok = 0, sids = 0, sprobs = 0, ns = 0, pending = 0, dstat = 0, dlse = 0, total = 0;
+};
+
+int plan_verify(const pm_rows* r, const pm_verify_args* v, VLayout* V) {
+  if (!r || !v || v->n_draft < 0 || r->rows < 0) return PM_ERR_ARG;
+  if (v->mode != PM_VERIFY_MATCH && v->mode != PM_VERIFY_RESIDUAL) return PM_ERR_ARG;
+  const int64_t K1 = (int64_t)v->n_draft + 1;
+  if (r->rows % K1) return PM_ERR_ARG;
+  int rc = plan(r, &V->L);
+  if (rc) return rc;
+  V->k = v->n_draft;
+  V->B = r->rows / K1;
+  const bool res = v->mode == PM_VERIFY_RESIDUAL;
+  V->D = res ? V->B * V->k : 0;
+  V->scap = res ? V->L.KC : 0;
+  const int64_t R = r->rows;
+  size_t o = V->L.total;
+  auto take = [&](size_t bytes) { o = align_up(o, 256); const size_t at = o; o += bytes; return at; };
+  V->rtok = take(sizeof(int32_t) * R);
+  V->sids = take(sizeof(int32_t) * R * V->scap);
+  V->sprobs = take(sizeof(float) * R * V->scap);
+  V->ns = take(sizeof(int32_t) * R);
+  V->pending = take(sizeof(int32_t) * V->B);
+  V->dstat = take(sizeof(pm::TileStat) * V->D * V->L.n_tiles);
+  V->dlse = take(sizeof(float) * V->D);
+  V->total = align_up(o, 256);
+  return PM_OK;
+}
+
+// Tile statistics and log-sum-exp of the raw draft rows (no processors).
+template <typename TD>
+int launch_draft_lse(const pm_rows* rows, const pm_verify_args* v, const VLayout& V, unsigned char* ws,
+                     cudaStream_t st) {
+  pm::SampleArgs da;
+  memset(&da, 0, sizeof(da));
+  da.logits = v->draft_logits;
+  da.rows = V.D;
+  da.vocab = rows->vocab;
+  da.row_stride = v->draft_row_stride;
+  da.vec_ok = ((uintptr_t)v->draft_logits % 16 == 0) && ((v->draft_row_stride * sizeof(TD)) % 16 == 0);
+  da.params = rows->params;  // only read when a tile has overrides, and the draft rows have none
+  da.params_per_row = 0;
+  da.n_tiles = V.L.n_tiles;
+  da.statx = reinterpret_cast<pm::TileStat*>(ws + V.dstat);
+  da.row_lse = reinterpret_cast<float*>(ws + V.dlse);
+  const int64_t work = V.D * (int64_t)V.L.n_tiles;
+  int64_t grid = (work + pm::kWarpsS - 1) / pm::kWarpsS;
+  if (grid > (int64_t)num_sms() * 16) grid = (int64_t)num_sms() * 16;
+  pm::k_process_rows<TD><<<(unsigned)grid, pm::kThreadsS, pm::kWarpsS * pm::kTile * 4, st>>>(da, nullptr, 0, true);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  int64_t g2 = (V.D + pm::kWarpsS - 1) / pm::kWarpsS;
+  if (g2 > (int64_t)num_sms() * 8) g2 = (int64_t)num_sms() * 8;
+  pm::k_row_lse<<<(unsigned)g2, pm::kThreadsS, 0, st>>>(da, nullptr);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? PM_OK : cuda_fail(e);
+}
+
+template <int KC>
+int launch_accept(const pm::SampleArgs& a, int dtype, const pm::VerifyK& vk, int64_t B, cudaStream_t st) {
+  constexpr int kAccWarps = 8;
+  const size_t smem = sizeof(uint64_t) * 2 * KC * kAccWarps;
+  int64_t grid = (B + kAccWarps - 1) / kAccWarps;
+  if (grid > (int64_t)num_sms() * 8) grid = (int64_t)num_sms() * 8;
+  pm::k_verify_accept<KC><<<(unsigned)grid, 32 * kAccWarps, smem, st>>>(a, dtype, vk);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PM_OK : cuda_fail(e);
 }
 
 }  // namespace
@@ -854,13 +956,9 @@ int pm_sample_rows(const pm_rows* rows, const pm_noise* noise, const pm_sample_o
                    size_t workspace_bytes, void* stream) {
   int rc = check_rows(rows);
   if (rc) return rc;
-  if (!noise || !out || !out->tokens || !workspace) return PM_ERR_ARG;
-  if (noise->mode != PM_NOISE_PHILOX && noise->mode != PM_NOISE_INJECTED) return PM_ERR_ARG;
-  if (noise->mode == PM_NOISE_INJECTED) {
-    const bool cand = rows->top_k_max > 0 || (rows->flags_any & (PM_F_TOP_P | PM_F_MIN_P));
-    if (cand && (!noise->gumbel || noise->gumbel_stride < rows->vocab)) return PM_ERR_ARG;
-    if ((rows->flags_any & PM_F_FULL) && !noise->uniform) return PM_ERR_ARG;
-  }
+  if (!out || !out->tokens || !workspace) return PM_ERR_ARG;
+  rc = check_noise(rows, noise);
+  if (rc) return rc;
   if (out->surv_ids && (!out->surv_probs || !out->n_surv || out->surv_cap <= 0)) return PM_ERR_ARG;
   Layout L;
   rc = plan(rows, &L);
@@ -873,13 +971,7 @@ int pm_sample_rows(const pm_rows* rows, const pm_noise* noise, const pm_sample_o
   memset(&a, 0, sizeof(a));
   rc = launch_prep(rows, L, ws, a, st);
   if (rc) return rc;
-  a.noise_mode = noise->mode;
-  a.seed = noise->seed;
-  a.offset = noise->offset;
-  a.row_base = noise->row_base;
-  a.gumbel = noise->gumbel;
-  a.gumbel_stride = noise->gumbel_stride;
-  a.uniform = noise->uniform;
+  set_noise(noise, a);
   a.tokens = out->tokens;
   a.lse_out = out->lse;
   a.tok_logprob = out->token_logprob;
@@ -888,7 +980,7 @@ int pm_sample_rows(const pm_rows* rows, const pm_noise* noise, const pm_sample_o
   a.n_surv = out->n_surv;
   a.surv_cap = out->surv_cap;
   a.want_lse = out->lse != nullptr || out->token_logprob != nullptr;
-  return launch_stream_any(rows->dtype, L.KC, a, st);
+  return launch_stream_any(rows->dtype, L.KC, a, has_cand_rows(rows), st);
 }
 
 size_t pm_processors_workspace_bytes(const pm_rows* rows) { return pm_sample_workspace_bytes(rows); }
@@ -944,6 +1036,86 @@ int pm_apply_processors(const pm_rows* rows, float* out, int64_t out_stride, voi
 int pm_logprobs(const pm_rows* rows, float* out, int64_t out_stride, float* lse_out, void* workspace,
                 size_t workspace_bytes, void* stream) {
   return process_common(rows, out, out_stride, lse_out, true, workspace, workspace_bytes, stream);
+}
+
+size_t pm_verify_workspace_bytes(const pm_rows* rows, const pm_verify_args* v) {
+  VLayout V;
+  if (plan_verify(rows, v, &V) != PM_OK) return 0;
+  return V.total;
+}
+
+int pm_verify(const pm_rows* rows, const pm_noise* noise, const pm_verify_args* v, void* workspace,
+              size_t workspace_bytes, void* stream) {
+  int rc = check_rows(rows);
+  if (rc) return rc;
+  if (!v || !workspace || !v->tokens || !v->n_accepted) return PM_ERR_ARG;
+  if (v->n_draft > 0 && !v->drafts) return PM_ERR_ARG;
+  if (rows->feed && rows->feed_group != v->n_draft + 1) return PM_ERR_ARG;
+  const bool res = v->mode == PM_VERIFY_RESIDUAL;
+  if (res && v->n_draft > 0) {
+    if (!v->draft_logits || v->draft_row_stride < rows->vocab) return PM_ERR_ARG;
+    if (v->draft_dtype != PM_DTYPE_F32 && v->draft_dtype != PM_DTYPE_BF16) return PM_ERR_ARG;
+  }
+  rc = check_noise(rows, noise);
+  if (rc) return rc;
+  VLayout V;
+  rc = plan_verify(rows, v, &V);
+  if (rc) return rc;
+  if (workspace_bytes < V.total) return PM_ERR_WORKSPACE;
+  if (rows->rows == 0) return PM_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  unsigned char* ws = reinterpret_cast<unsigned char*>(workspace);
+  if (V.D > 0) {
+    rc = v->draft_dtype == PM_DTYPE_BF16 ? launch_draft_lse<__nv_bfloat16>(rows, v, V, ws, st)
+                                         : launch_draft_lse<float>(rows, v, V, ws, st);
+    if (rc) return rc;
+  }
+  pm::SampleArgs a;
+  memset(&a, 0, sizeof(a));
+  rc = launch_prep(rows, V.L, ws, a, st);
+  if (rc) return rc;
+  set_noise(noise, a);
+  a.tokens = reinterpret_cast<int32_t*>(ws + V.rtok);
+  a.n_surv = reinterpret_cast<int32_t*>(ws + V.ns);
+  if (res) {
+    a.surv_ids = reinterpret_cast<int32_t*>(ws + V.sids);
+    a.surv_probs = reinterpret_cast<float*>(ws + V.sprobs);
+    a.surv_cap = V.scap;
+  }
+  rc = launch_stream_any(rows->dtype, V.L.KC, a, has_cand_rows(rows), st);
+  if (rc) return rc;
+  pm::VerifyK vk;
+  memset(&vk, 0, sizeof(vk));
+  vk.mode = v->mode;
+  vk.drafts = v->drafts;
+  vk.k = v->n_draft;
+  vk.dlogits = v->draft_logits;
+  vk.ddtype = v->draft_dtype;
+  vk.dstride = v->draft_row_stride;
+  vk.dlse = reinterpret_cast<const float*>(ws + V.dlse);
+  vk.u_accept = v->u_accept;
+  vk.u_residual = v->u_residual;
+  vk.tokens = v->tokens;
+  vk.n_acc = v->n_accepted;
+  vk.row_tokens = v->row_tokens;
+  vk.rtok = a.tokens;
+  vk.sids = a.surv_ids;
+  vk.sprobs = a.surv_probs;
+  vk.ns = a.n_surv;
+  vk.scap = V.scap;
+  vk.pending = reinterpret_cast<int32_t*>(ws + V.pending);
+  rc = V.L.KC == 64 ? launch_accept<64>(a, rows->dtype, vk, V.B, st) : launch_accept<256>(a, rows->dtype, vk, V.B, st);
+  if (rc) return rc;
+  if (res && V.k > 0 && (rows->flags_any & PM_F_FULL)) {
+    int64_t grid = V.B < (int64_t)num_sms() * 4 ? V.B : (int64_t)num_sms() * 4;
+    if (rows->dtype == PM_DTYPE_BF16)
+      pm::k_verify_residual<__nv_bfloat16><<<(unsigned)grid, 256, 0, st>>>(a, vk);
+    else
+      pm::k_verify_residual<float><<<(unsigned)grid, 256, 0, st>>>(a, vk);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
+  return PM_OK;
 }
 
 }  // extern "C"

@@ -61,7 +61,6 @@ struct SampleArgs {
   uint64_t* cand;    // [rows, max_parts, KC] candidate keys of each row part
   int32_t* cand_n;   // [rows, max_parts] count | (1 << 30) when the part was trimmed
   uint64_t* best;    // [rows, max_parts] greedy best key of each row part
-  uint32_t* row_done;
   uint64_t* row_tau;   // [rows] largest K-th key any part of the row has proven (0: none)
   int32_t* status;   // [rows] 0 ok, 1 survivors beyond the candidates, 2 history window too long
   bool prep_ran;     // the override prep wrote status this call

@@ -1,0 +1,337 @@
+// pm_verify_impl.cuh -- draft acceptance of a verify pass (included at the
+// end of pm_sample.cu: it reuses that file's kernels and host planning).
+//
+// The target rows of every request go through the same fused streaming and
+// merge kernels as plain sampling (their processors see history + [y] +
+// drafts[:i] through the feed), writing each row's sample (and, in residual
+// mode, its survivors) to the workspace.  Then:
+//   match mode    (reference lookup_decode.py:363-369, verify_decode.py:915-921)
+//                 a warp per request keeps the drafts while they equal the
+//                 rows' own samples and emits samples[:accepted + 1];
+//   residual mode (speculative sampling, Leviathan et al. 2023; not in the
+//                 reference) a warp per request accepts draft i when
+//                 u_i q_i(d_i) < p_i(d_i) (fp64) and, at the first rejection,
+//                 draws from max(fl32(p - q), 0) by the exact fixed-point
+//                 inverse CDF in ascending token order: over the survivors
+//                 when the sampler filters, one-hot when greedy, and over the
+//                 whole vocabulary (a CTA re-streams the row pair) otherwise.
+#pragma once
+
+namespace pm {
+
+struct VerifyK {
+  int32_t mode;
+  const int32_t* drafts;   // [B, k]
+  int32_t k;
+  const void* dlogits;     // [B*k, dstride] raw draft logits
+  int32_t ddtype;
+  int64_t dstride;
+  const float* dlse;       // [B*k] log-sum-exp of the draft rows
+  const double* u_accept;  // [B, k] or null (Philox stream 2)
+  const double* u_residual;  // [B] or null (Philox stream 3)
+  int32_t* tokens;         // [B, k+1], -1 padded
+  int32_t* n_acc;          // [B]
+  int32_t* row_tokens;     // optional [B*(k+1)] every row's own sample
+  const int32_t* rtok;     // [B*(k+1)] the rows' samples (workspace)
+  const int32_t* sids;     // [B*(k+1), scap] survivors in rank order
+  const float* sprobs;
+  const int32_t* ns;       // [B*(k+1)]
+  int32_t scap;
+  int32_t* pending;        // [B] row awaiting a whole-vocabulary residual draw, -1 if none
+};
+
+__device__ __forceinline__ float draft_value(const VerifyK& v, int64_t drow, int64_t tok) {
+  if (v.ddtype == PM_DTYPE_F32) return reinterpret_cast<const float*>(v.dlogits)[drow * v.dstride + tok];
+  return bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(v.dlogits)[drow * v.dstride + tok]);
+}
+
+// q(tok) = expf(fl32(d - lse_d)) of a draft row.
+__device__ __forceinline__ float draft_prob(const VerifyK& v, int64_t drow, int64_t tok, float cd) {
+  return det_expf(fsub(draft_value(v, drow, tok), cd));
+}
+
+// floor(max(fl32(p - q), 0) 2^52); the scaling by 2^52 is exact.
+__device__ __forceinline__ uint64_t residual_q52(float p, float q) {
+  const float r = fsub(p, q);
+  return r > 0.0f ? __float2ull_rz(fmul(r, 0x1p52f)) : 0ull;
+}
+
+// The processed logit of one token of a row (bias, penalties, mask): the
+// single-token form of process_tile.
+__device__ float processed_value(const SampleArgs& a, int dtype, const pm_row_params& p, int64_t row, int tok) {
+  float x;
+  if (dtype == PM_DTYPE_F32) x = reinterpret_cast<const float*>(a.logits)[row * a.row_stride + tok];
+  else x = bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(a.logits)[row * a.row_stride + tok]);
+  const int tile = tok / kTile;
+  if (a.bias_off)
+    for (int i = a.bias_off[tile]; i < a.bias_off[tile + 1]; ++i)
+      if (a.bias_tok[i] == tok) x = fadd(x, a.bias_val[i]);
+  if (a.ovr_off) {
+    const int32_t* off = a.ovr_off + row * (int64_t)(a.n_tiles + 1) + tile;
+    const int32_t* otok = a.ovr_tok + row * (int64_t)a.ovr_cap;
+    int lo = off[0], hi = off[1];
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (otok[mid] < tok) lo = mid + 1; else hi = mid;
+    }
+    if (lo < off[1] && otok[lo] == tok) {
+      const uint32_t info = a.ovr_info[row * (int64_t)a.ovr_cap + lo];
+      if (info & 1u) x = x < 0.0f ? fmul(x, p.repetition_penalty) : __fdiv_rn(x, p.repetition_penalty);
+      if (info & 2u) x = fsub(x, p.presence_penalty);
+      const uint32_t cnt = info >> 8;
+      if (cnt) x = fsub(x, fmul(p.frequency_penalty, (float)cnt));
+    }
+  }
+  if (a.mask && !((a.mask[row * a.mask_stride + (tok >> 5)] >> (tok & 31)) & 1u)) x = -INFINITY;
+  return x;
+}
+
+__device__ __forceinline__ double accept_uniform(const SampleArgs& a, const VerifyK& v, int64_t b, int i,
+                                                 int64_t row) {
+  if (v.u_accept) return v.u_accept[b * v.k + i];
+  return dmul((double)philox_u53(a.seed, a.offset, a.row_base + (uint32_t)row, 2), 0x1p-53);
+}
+
+__device__ __forceinline__ uint64_t residual_u53(const SampleArgs& a, const VerifyK& v, int64_t b, int64_t row) {
+  if (v.u_residual) return u53_from_double(v.u_residual[b]);
+  return philox_u53(a.seed, a.offset, a.row_base + (uint32_t)row, 3);
+}
+
+// Residual draw over a filtered row's survivors, ascending token order.
+// Returns -1 when no survivor has a positive residual.
+template <int KC>
+__device__ int survivor_residual(const SampleArgs& a, const VerifyK& v, int64_t b, int64_t row, int64_t drow,
+                                 float cd, uint64_t* key, uint64_t* q) {
+  const int lane = threadIdx.x & 31;
+  const int n = ld_cg(&v.ns[row]);
+  uint64_t R = 0;
+  for (int r = lane; r < n; r += 32) {
+    const int id = ld_cg(&v.sids[row * v.scap + r]);
+    const uint64_t qq = residual_q52(ld_cg(&v.sprobs[row * v.scap + r]), draft_prob(v, drow, id, cd));
+    key[r] = ((uint64_t)(0xFFFFFFFFu - (uint32_t)id) << 32) | (uint32_t)r;  // descending key = ascending id
+    q[r] = qq;
+    R += qq;
+  }
+  R = warp_sum_u64(R);
+  __syncwarp();
+  if (R == 0) return -1;
+  warp_sort_desc(key, n);
+  const uint64_t tgt = scale_u53(residual_u53(a, v, b, row), R);
+  uint64_t carry = 0;
+  for (int r0 = 0; r0 < n; r0 += 32) {
+    const int r = r0 + lane;
+    const uint64_t kk = r < n ? key[r] : 0ull;
+    const uint64_t qq = r < n ? q[(uint32_t)kk] : 0ull;
+    const uint64_t incl = carry + warp_incl_scan_u64(qq);
+    const unsigned hit = __ballot_sync(kFull, r < n && incl > tgt);
+    if (hit) {
+      const uint64_t kh = __shfl_sync(kFull, kk, __ffs(hit) - 1);
+      __syncwarp();
+      return (int)(0xFFFFFFFFu - (uint32_t)(kh >> 32));
+    }
+    carry = __shfl_sync(kFull, incl, 31);
+  }
+  __syncwarp();
+  return -1;
+}
+
+// Acceptance: one warp per request.
+template <int KC>
+__global__ void __launch_bounds__(256) k_verify_accept(const __grid_constant__ SampleArgs a, int dtype,
+                                                       const __grid_constant__ VerifyK v) {
+  struct AccMem {
+    uint64_t key[KC];
+    uint64_t q[KC];
+  };
+  extern __shared__ __align__(16) unsigned char smem_acc[];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  AccMem* am = reinterpret_cast<AccMem*>(smem_acc) + wid;
+  const int K1 = v.k + 1;
+  const int64_t B = a.rows / K1;
+  for (int64_t b = (int64_t)blockIdx.x * (blockDim.x >> 5) + wid; b < B;
+       b += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    const int64_t base = b * K1;
+    int32_t* out = v.tokens + b * K1;
+    if (v.row_tokens)
+      for (int i = lane; i < K1; i += 32) v.row_tokens[base + i] = ld_cg(&v.rtok[base + i]);
+    if (v.mode == PM_VERIFY_MATCH) {
+      int emit = K1;
+      for (int i0 = 0; i0 < K1; i0 += 32) {
+        const int i = i0 + lane;
+        bool stop = false;
+        if (i < K1) stop = i == v.k || ld_cg(&v.rtok[base + i]) != v.drafts[b * v.k + i];
+        const unsigned bal = __ballot_sync(kFull, stop);
+        if (bal) { emit = i0 + __ffs(bal); break; }
+      }
+      for (int i = lane; i < K1; i += 32) out[i] = i < emit ? ld_cg(&v.rtok[base + i]) : -1;
+      if (lane == 0) { v.n_acc[b] = emit - 1; v.pending[b] = -1; }
+      __syncwarp();
+      continue;
+    }
+    int i = 0;
+    int final_tok = 0;
+    bool pend = false;
+    for (; i < v.k; ++i) {
+      const int64_t row = base + i;
+      const int64_t drow = b * v.k + i;
+      const pm_row_params p = row_params(a, row);
+      const int mode = row_mode(p);
+      const int d = v.drafts[b * v.k + i];
+      const float cd = ld_cg(&v.dlse[drow]);
+      const float q_d = draft_prob(v, drow, d, cd);
+      float p_d;
+      if (mode == kGreedy) {
+        p_d = ld_cg(&v.rtok[row]) == d ? 1.0f : 0.0f;
+      } else if (mode == kCand) {
+        const int n = ld_cg(&v.ns[row]);
+        float f = 0.0f;
+        for (int r = lane; r < n; r += 32)
+          if (ld_cg(&v.sids[row * v.scap + r]) == d) f = ld_cg(&v.sprobs[row * v.scap + r]);
+        p_d = warp_max(f);
+      } else {
+        float m;
+        const float cy = warp_combine(a.staty + row * a.n_tiles, a.n_tiles, &m);
+        const float x = processed_value(a, dtype, p, row, d);
+        const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
+        p_d = det_expf(fsub(y, cy));
+      }
+      if (dmul(accept_uniform(a, v, b, i, row), (double)q_d) < (double)p_d) continue;
+      // first rejection at row i: a draw from max(p - q, 0)
+      if (mode == kGreedy) {
+        final_tok = ld_cg(&v.rtok[row]);  // the only token with a positive residual, or the row's own draw
+      } else if (mode == kCand) {
+        final_tok = survivor_residual<KC>(a, v, b, row, drow, cd, am->key, am->q);
+        if (final_tok < 0) final_tok = ld_cg(&v.rtok[row]);
+      } else {
+        pend = true;  // whole vocabulary: k_verify_residual draws it
+      }
+      break;
+    }
+    if (i == v.k) final_tok = ld_cg(&v.rtok[base + v.k]);  // every draft accepted: the bonus token
+    for (int r = lane; r < K1; r += 32)
+      out[r] = r < i ? v.drafts[b * v.k + r] : (r == i && !pend ? final_tok : -1);
+    if (lane == 0) { v.n_acc[b] = i; v.pending[b] = pend ? i : -1; }
+    __syncwarp();
+  }
+}
+
+// Whole-vocabulary residual draw: one CTA per request with a pending row.
+// Tile sums of floor(max(fl32(p - q), 0) 2^52), p = expf(fl32(y - c_y)),
+// q = expf(fl32(d - c_d)); the token is the first (ascending) whose inclusive
+// prefix exceeds floor(u R).  No positive residual: the row's own draw.
+template <typename T>
+__global__ void __launch_bounds__(256) k_verify_residual(const __grid_constant__ SampleArgs a,
+                                                         const __grid_constant__ VerifyK v) {
+  constexpr int VW = Lay<T>::VW;
+  __shared__ uint64_t tsum[32 * kMaxPer];
+  __shared__ float s_cy;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int K1 = v.k + 1;
+  const int64_t B = a.rows / K1;
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    const int j = ld_cg(&v.pending[b]);
+    if (j < 0) continue;  // uniform across the CTA
+    const int64_t row = b * K1 + j;
+    const int64_t drow = b * v.k + j;
+    const pm_row_params p = row_params(a, row);
+    if (wid == 0) {
+      float m;
+      const float cy = warp_combine(a.staty + row * a.n_tiles, a.n_tiles, &m);
+      if (lane == 0) s_cy = cy;
+    }
+    __syncthreads();
+    const float cy = s_cy;
+    const float cd = ld_cg(&v.dlse[drow]);
+    for (int t = wid; t < a.n_tiles; t += nw) {
+      TileIn ti;
+      load_tile<T>(a, row, t, ti);
+      process_tile_regs<VW>(a, p, row, t, ti);
+      const int64_t start = (int64_t)t * kTile;
+      const int n_valid = tile_valid(a, t);
+      uint64_t s = 0;
+#pragma unroll
+      for (int sl = 0; sl < 32; ++sl) {
+        const int e = slot_elem<VW>(sl, lane);
+        if (e < n_valid) {
+          const float x = ti.v[sl];
+          const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
+          s += residual_q52(det_expf(fsub(y, cy)), draft_prob(v, drow, start + e, cd));
+        }
+      }
+      s = warp_sum_u64(s);
+      if (lane == 0) tsum[t] = s;
+    }
+    __syncthreads();
+    if (wid == 0) {
+      uint64_t R = 0;
+      for (int t = lane; t < a.n_tiles; t += 32) R += tsum[t];
+      R = warp_sum_u64(R);
+      int tt = -1;
+      uint64_t t2 = 0;
+      if (R > 0) {
+        const uint64_t tgt = scale_u53(residual_u53(a, v, b, row), R);
+        uint64_t carry = 0;
+        for (int t0 = 0; t0 < a.n_tiles; t0 += 32) {
+          const int t = t0 + lane;
+          const uint64_t w = t < a.n_tiles ? tsum[t] : 0ull;
+          const uint64_t incl = carry + warp_incl_scan_u64(w);
+          const unsigned hit = __ballot_sync(kFull, t < a.n_tiles && incl > tgt);
+          if (hit) {
+            const int src = __ffs(hit) - 1;
+            tt = t0 + src;
+            t2 = tgt - (__shfl_sync(kFull, incl, src) - __shfl_sync(kFull, w, src));
+            break;
+          }
+          carry = __shfl_sync(kFull, incl, 31);
+        }
+      }
+      int tok = ld_cg(&v.rtok[row]);
+      if (tt >= 0) {
+        TileIn ti;
+        load_tile<T>(a, row, tt, ti);
+        process_tile_regs<VW>(a, p, row, tt, ti);
+        const int64_t start = (int64_t)tt * kTile;
+        const int n_valid = tile_valid(a, tt);
+        uint64_t acc = 0;
+        for (int jj = 0; jj < 32 / VW; ++jj) {
+          uint64_t q[VW];
+          uint64_t ls = 0;
+#pragma unroll
+          for (int c = 0; c < VW; ++c) {
+            const int e = jj * 32 * VW + lane * VW + c;
+            q[c] = 0;
+            if (e < n_valid) {
+              const float x = ti.v[jj * VW + c];
+              const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
+              q[c] = residual_q52(det_expf(fsub(y, cy)), draft_prob(v, drow, start + e, cd));
+            }
+            ls += q[c];
+          }
+          const uint64_t incl = acc + warp_incl_scan_u64(ls);
+          const unsigned hit = __ballot_sync(kFull, incl > t2);
+          if (hit) {
+            const int src = __ffs(hit) - 1;
+            int found = 0;
+            if (lane == src) {
+              uint64_t run = incl - ls;
+              found = -1;
+#pragma unroll
+              for (int c = 0; c < VW; ++c) {
+                run += q[c];
+                if (found < 0 && run > t2) found = c;
+              }
+            }
+            found = __shfl_sync(kFull, found, src);
+            tok = (int)(start + jj * 32 * VW + src * VW + found);
+            break;
+          }
+          acc = __shfl_sync(kFull, incl, 31);
+        }
+      }
+      if (lane == 0) v.tokens[b * K1 + j] = tok;
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace pm

@@ -131,28 +131,62 @@ __device__ __forceinline__ double tile_weight(const TileStat* st, int t, float m
   return dmul((double)s, det_exp64(dsub((double)ld_cg(&st[t].m), (double)m)));
 }
 
+// A lane's share of a row's tile statistics, loaded with all loads in flight
+// at once: lane L holds tiles [L*per, L*per + per) of the row padded to
+// P = 32 * per tiles (per = 1..kMaxPer; rows of up to 32 * kMaxPer tiles).
+constexpr int kMaxPer = 8;  // rows of up to 256 tiles (262,144 tokens)
+
+struct LaneTiles {
+  int per;            // tiles per lane (a power of two)
+  int nt;
+  float m[kMaxPer];
+  uint64_t s[kMaxPer];
+};
+
+__device__ __forceinline__ void load_lane_tiles(const TileStat* st, int nt, LaneTiles& lt) {
+  const int lane = threadIdx.x & 31;
+  int P = 32;
+  while (P < nt) P <<= 1;
+  lt.per = P >> 5;
+  lt.nt = nt;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int t = lane * lt.per + i;
+    const bool ok = i < lt.per && t < nt;
+    lt.m[i] = ok ? ld_cg(&st[t].m) : -INFINITY;
+    lt.s[i] = ok ? ld_cg(&st[t].s) : 0ull;
+  }
+}
+
+__device__ __forceinline__ float lane_tiles_max(const LaneTiles& lt) {
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) m = fmaxf(m, lt.m[i]);
+  return warp_max(m);
+}
+
+__device__ __forceinline__ double tile_weight_of(float mt, uint64_t s, float m) {
+  if (!s) return 0.0;
+  return dmul((double)s, det_exp64(dsub((double)mt, (double)m)));
+}
+
 // Row log-sum-exp from its tile statistics, one warp:
 //   m = max_t m_t,  Z = pairwise sum over t of s_t e^(m_t - m)  (tiles padded
 //   with zeros to a power of two; lane L sums its contiguous block of P/32
 //   tiles as a complete subtree, then the lanes combine pairwise),
 //   c = fl32(m + log(Z 2^-52)).  -inf when no tile has a finite value.
-__device__ __forceinline__ float warp_combine(const TileStat* st, int nt, float* m_out) {
+__device__ __forceinline__ float combine_lane_tiles(const LaneTiles& lt, float m) {
   const int lane = threadIdx.x & 31;
-  float m = -INFINITY;
-  for (int t = lane; t < nt; t += 32) m = fmaxf(m, ld_cg(&st[t].m));
-  m = warp_max(m);
-  *m_out = m;
   if (!(m > -INFINITY)) return -INFINITY;
-  int P = 32;
-  while (P < nt) P <<= 1;
-  const int per = P >> 5;
-  double stk[12];
+  double stk[6];
   int sp = 0;
-  for (int i = 0; i < per; ++i) {
-    const int t = lane * per + i;
-    double v = t < nt ? tile_weight(st, t, m) : 0.0;
-    for (int c = i + 1; (c & 1) == 0; c >>= 1) v = dadd(stk[--sp], v);
-    stk[sp++] = v;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    if (i < lt.per) {
+      double v = tile_weight_of(lt.m[i], lt.s[i], m);
+      for (int c = i + 1; (c & 1) == 0; c >>= 1) v = dadd(stk[--sp], v);
+      stk[sp++] = v;
+    }
   }
   double acc = stk[0];
 #pragma unroll
@@ -162,6 +196,14 @@ __device__ __forceinline__ float warp_combine(const TileStat* st, int nt, float*
   }
   const double Z = __shfl_sync(kFull, acc, 0);
   return (float)dadd((double)m, det_log64(dmul(Z, 0x1p-52)));
+}
+
+__device__ __forceinline__ float warp_combine(const TileStat* st, int nt, float* m_out) {
+  LaneTiles lt;
+  load_lane_tiles(st, nt, lt);
+  const float m = lane_tiles_max(lt);
+  *m_out = m;
+  return combine_lane_tiles(lt, m);
 }
 
 __device__ __forceinline__ float row_gumbel(const SampleArgs& a, int64_t row, uint32_t token) {
@@ -328,31 +370,41 @@ __device__ __noinline__ int warp_full_draw(const SampleArgs& a, const pm_row_par
   const int lane = threadIdx.x & 31;
   const int nt = a.n_tiles;
   const TileStat* st = a.staty + row * (int64_t)nt;
-  float my;
-  {
-    float m = -INFINITY;
-    for (int t = lane; t < nt; t += 32) m = fmaxf(m, ld_cg(&st[t].m));
-    my = warp_max(m);
-  }
+  LaneTiles lt;
+  load_lane_tiles(st, nt, lt);
+  const float my = lane_tiles_max(lt);
   *x_out = -INFINITY;
   if (!(my > -INFINITY)) return 0;
   int sh = 1;
   while ((1 << (sh - 1)) < nt) ++sh;
   const double scale = __longlong_as_double((long long)(1023 - sh) << 52);  // 2^-sh
-  uint64_t W = 0;
-  for (int t = lane; t < nt; t += 32) W += __double2ull_rz(dmul(tile_weight(st, t, my), scale));
-  W = warp_sum_u64(W);
-  const uint64_t t1 = scale_u53(row_u53(a, row, 0), W);
-  int tt = nt - 1;
-  uint64_t carry = 0;
-  for (int base = 0; base < nt; base += 32) {
-    const int t = base + lane;
-    const uint64_t w = t < nt ? __double2ull_rz(dmul(tile_weight(st, t, my), scale)) : 0ull;
-    const uint64_t incl = carry + warp_incl_scan_u64(w);
-    const unsigned hit = __ballot_sync(kFull, t < nt && incl > t1);
-    if (hit) { tt = base + __ffs(hit) - 1; break; }
-    carry = __shfl_sync(kFull, incl, 31);
+  // tile weights of this lane's contiguous block, their sum, and the warp's
+  // exclusive prefix (lanes hold consecutive blocks, so block order = tile order)
+  uint64_t w[kMaxPer];
+  uint64_t lsum = 0;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    w[i] = i < lt.per ? __double2ull_rz(dmul(tile_weight_of(lt.m[i], lt.s[i], my), scale)) : 0ull;
+    lsum += w[i];
   }
+  const uint64_t incl = warp_incl_scan_u64(lsum);
+  const uint64_t W = __shfl_sync(kFull, incl, 31);
+  const uint64_t t1 = scale_u53(row_u53(a, row, 0), W);
+  const unsigned hit = __ballot_sync(kFull, incl > t1);
+  const int src = hit ? __ffs(hit) - 1 : 31;
+  int tt = nt - 1;
+  if (lane == src) {
+    uint64_t run = incl - lsum;
+    int found = -1;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      run += w[i];
+      if (found < 0 && i < lt.per && run > t1) found = i;
+    }
+    tt = lane * lt.per + (found < 0 ? 0 : found);
+  }
+  tt = __shfl_sync(kFull, tt, src);
+  if (tt >= nt) tt = nt - 1;
   const float mt = ld_cg(&st[tt].m);
   const uint64_t t2 = scale_u53(row_u53(a, row, 1), ld_cg(&st[tt].s));
   const int64_t start = (int64_t)tt * kTile;

@@ -234,9 +234,8 @@ def sample_rows(logits: torch.Tensor, sampler: Union[SamplerSettings, Sequence[S
 
 
 def status_view(ws: torch.Tensor, r: L.Rows) -> torch.Tensor:
-    # the status array sits right after the row counters (256-byte aligned)
-    off = ((4 * r.rows + 255) // 256) * 256
-    return ws[off: off + 4 * r.rows].view(torch.int32).clone()
+    # the status array opens the workspace
+    return ws[: 4 * r.rows].view(torch.int32).clone()
 
 
 def apply_processors(logits: torch.Tensor, processors=None, history=None, history_len=None, mask=None,
