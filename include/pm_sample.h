@@ -193,6 +193,21 @@ PM_API size_t pm_verify_workspace_bytes(const pm_rows *rows, const pm_verify_arg
 PM_API int pm_verify(const pm_rows *rows, const pm_noise *noise, const pm_verify_args *v, void *workspace,
                      size_t workspace_bytes, void *stream);
 
+/* pm_sample_rows on scratch owned by the library (no counterpart in the
+ * reference, which runs on MLX's allocator): for callers that cannot hand
+ * over a device workspace or must not allocate between decode steps.
+ * The scratch is a fixed device array of PM_STATIC_SCRATCH_BYTES per device;
+ * a call whose rows need more (pm_sample_workspace_bytes(rows) larger than
+ * that) returns PM_ERR_WORKSPACE and does nothing: use pm_sample_rows with a
+ * workspace of that size instead.  The first call on a device looks the
+ * scratch address up, so make it before any stream capture.  Nothing in the
+ * scratch needs to start at zero.  One scratch per device: calls on the same
+ * device must not overlap (they race on it); keep them on one stream or
+ * serialise them. */
+#define PM_STATIC_SCRATCH_BYTES (32u << 20)
+PM_API int pm_sample_rows_static(const pm_rows *rows, const pm_noise *noise, const pm_sample_out *out,
+                                 void *stream);
+
 /* Last CUDA error seen by this thread (cudaError_t value), 0 if none. */
 PM_API int pm_last_cuda_error(void);
 

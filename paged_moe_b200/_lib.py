@@ -33,6 +33,8 @@ PM_F_FREQ = 0x40
 PM_F_UNBOUNDED = 0x100
 PM_F_FULL = 0x200
 
+PM_STATIC_SCRATCH_BYTES = 32 << 20
+
 PM_VERIFY_MATCH = 0
 PM_VERIFY_RESIDUAL = 1
 
@@ -104,6 +106,7 @@ SIGNATURES = {
     "pm_last_cuda_error": (C.c_int, []),
     "pm_sample_workspace_bytes": (C.c_size_t, [_P]),
     "pm_sample_rows": (C.c_int, [_P, _P, _P, _P, C.c_size_t, _P]),
+    "pm_sample_rows_static": (C.c_int, [_P, _P, _P, _P]),
     "pm_processors_workspace_bytes": (C.c_size_t, [_P]),
     "pm_apply_processors": (C.c_int, [_P, _P, C.c_int64, _P, C.c_size_t, _P]),
     "pm_logprobs": (C.c_int, [_P, _P, C.c_int64, _P, _P, C.c_size_t, _P]),

@@ -1119,3 +1119,60 @@ int pm_verify(const pm_rows* rows, const pm_noise* noise, const pm_verify_args* 
 }
 
 }  // extern "C"
+
+// ============================================================================
+// Fixed-scratch variant of pm_sample_rows
+// ============================================================================
+// Some callers have no device allocator to take a workspace from: a host
+// binding (cgo, JNI, a C server loop) that holds only the logits and output
+// pointers, or a decode loop that must not call cudaMalloc between steps
+// because it synchronises the whole device and stalls the other streams.
+// For them the sampling pass can run out of scratch that the library owns: a
+// file-scope device array, placed in device memory by the CUDA driver when it
+// loads this module, never by a call.  Its address is looked up once per
+// device (cudaGetSymbolAddress with that device current) on the first call
+// there, so that first call should come before any stream capture.  Nothing
+// in it needs to start at zero: the pass zeroes the row thresholds itself
+// (cudaMemsetAsync on the caller's stream) and writes every other byte
+// before reading it.  There is one scratch array per device, so calls on the
+// same device must not overlap (one stream, or serialised by the caller);
+// overlapping calls race on it.
+namespace {
+
+static __device__ __align__(256) unsigned char g_static_scratch[PM_STATIC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_ptr[kMaxDevices] = {};
+
+int static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (dev < 0 || dev >= kMaxDevices) return PM_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e);
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return PM_OK;
+}
+
+}  // namespace
+
+extern "C" int pm_sample_rows_static(const pm_rows* rows, const pm_noise* noise, const pm_sample_out* out,
+                                     void* stream) {
+  int rc = check_rows(rows);
+  if (rc) return rc;
+  Layout L;
+  rc = plan(rows, &L);
+  if (rc) return rc;
+  if (L.total > (size_t)PM_STATIC_SCRATCH_BYTES) return PM_ERR_WORKSPACE;
+  void* ws = nullptr;
+  rc = static_scratch(&ws);
+  if (rc) return rc;
+  return pm_sample_rows(rows, noise, out, ws, (size_t)PM_STATIC_SCRATCH_BYTES, stream);
+}
