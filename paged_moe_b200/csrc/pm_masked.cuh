@@ -1,0 +1,539 @@
+// pm_masked.cuh -- the sampling pass for rows with an allowed-token mask,
+// one CTA per row.
+//
+// A constrained-decoding mask usually allows a small part of the vocabulary
+// (a grammar state, a forced token).  Every processed value of a disallowed
+// token is -inf and contributes nothing to the row's log-sum-exp, candidates
+// or draw, so this pass reads the row's mask words first and then fetches
+// only the logits of allowed tokens: asynchronous 4-byte copies
+// (cp.async, L2 evict-first) into a shared-memory window, compacted in
+// ascending token order.  The HBM traffic is the mask plus the 32-byte
+// sectors that hold an allowed token, instead of the whole row.
+//
+// Per row (8 warps, one CTA):
+//   1. mask words -> shared memory (cut at the vocabulary), allowed count per
+//      1024-token tile, their prefix (tile offsets in the row's list);
+//   2. windows of whole tiles holding at most kWin allowed tokens: gather,
+//      keys rankkey(x, id), processors on the few overridden ids, exact tile
+//      statistics (the same 1024-token tiles as every other pass, so the
+//      log-sum-exp is bit-identical), selection: the window's keys above the
+//      running K-th key join the carried top-K, radix-selected back to K;
+//   3. the draw by warp 0: greedy argmax, filters + Gumbel-max over the
+//      sorted top-K, or the two-level inverse CDF over the y statistics.
+// Results, tie rules and noise are those of the streaming pass.
+#pragma once
+
+namespace pm {
+
+constexpr int kMThreads = 256;
+constexpr int kMWarps = kMThreads / 32;
+constexpr int kWin = 4096;                          // allowed tokens per window
+constexpr int kMaxTiles = 32 * kMaxPer;             // tiles of the largest row (256)
+constexpr int kMaxWords = kMaxTiles * 32;           // mask words of the largest row (8192)
+constexpr int kSel = 1024;                          // keys the fast selection path holds
+
+template <int KC>
+struct MaskedMem {
+  uint32_t val[kWin];         // gathered raw words, then the processed fp32 values (bits), by position
+  uint32_t ids[kWin];         // token id of each position
+  uint32_t mw[kMaxWords];     // the row's mask words
+  uint16_t wpre[kMaxWords];   // allowed tokens before each word inside its tile
+  uint64_t sel[kSel + KC];    // selection buffer
+  uint64_t carry[KC];         // the row's top-K so far, sorted descending
+  uint32_t tmx[kMaxTiles];    // tile maxima of x as ordered keys (0: nothing finite)
+  uint32_t tmy[kMaxTiles];    // tile maxima of y = x * inv_temperature
+  uint64_t tsx[kMaxTiles];    // tile sums of q52(x - m_t)
+  uint64_t tsy[kMaxTiles];
+  int toff[kMaxTiles + 1];    // allowed tokens before each tile
+  unsigned hist[256];
+  int scal[8];
+  uint64_t wbest[kMWarps];
+  float score[KC];            // Gumbel scores of the carried keys
+  int nsel;
+  float v0;
+  float lse;
+};
+
+__device__ __forceinline__ float ord_value(uint32_t o) {
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o);
+}
+
+// Segmented reductions over lanes whose segment ids are contiguous runs
+// (positions sorted by token, segments = tiles): the first lane of each run
+// ends up with the run's total.
+__device__ __forceinline__ uint32_t seg_max_u32(uint32_t v, int seg) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t ov = __shfl_down_sync(kFull, v, o);
+    const int os = __shfl_down_sync(kFull, seg, o);
+    if (lane + o < 32 && os == seg) v = max(v, ov);
+  }
+  return v;
+}
+__device__ __forceinline__ uint64_t seg_sum_u64(uint64_t v, int seg) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint64_t ov = __shfl_down_sync(kFull, v, o);
+    const int os = __shfl_down_sync(kFull, seg, o);
+    if (lane + o < 32 && os == seg) v += ov;
+  }
+  return v;
+}
+__device__ __forceinline__ bool seg_head(int seg) {
+  const int prev = __shfl_up_sync(kFull, seg, 1);
+  return (threadIdx.x & 31) == 0 || prev != seg;
+}
+
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, uint64_t policy) {
+  asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "l"(policy)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// The processed logit of one token of a row (bias, penalties, mask): the
+// single-token form of process_tile, for the rare paths.
+__device__ float processed_value(const SampleArgs& a, int dtype, const pm_row_params& p, int64_t row, int tok) {
+  float x;
+  if (dtype == PM_DTYPE_F32) x = reinterpret_cast<const float*>(a.logits)[row * a.row_stride + tok];
+  else x = bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(a.logits)[row * a.row_stride + tok]);
+  const int tile = tok / kTile;
+  if (a.bias_off)
+    for (int i = a.bias_off[tile]; i < a.bias_off[tile + 1]; ++i)
+      if (a.bias_tok[i] == tok) x = fadd(x, a.bias_val[i]);
+  if (a.ovr_off) {
+    const int32_t* off = a.ovr_off + row * (int64_t)(a.n_tiles + 1) + tile;
+    const int32_t* otok = a.ovr_tok + row * (int64_t)a.ovr_cap;
+    int lo = off[0], hi = off[1];
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (otok[mid] < tok) lo = mid + 1; else hi = mid;
+    }
+    if (lo < off[1] && otok[lo] == tok) {
+      const uint32_t info = a.ovr_info[row * (int64_t)a.ovr_cap + lo];
+      if (info & 1u) x = x < 0.0f ? fmul(x, p.repetition_penalty) : __fdiv_rn(x, p.repetition_penalty);
+      if (info & 2u) x = fsub(x, p.presence_penalty);
+      const uint32_t cnt = info >> 8;
+      if (cnt) x = fsub(x, fmul(p.frequency_penalty, (float)cnt));
+    }
+  }
+  if (a.mask && !((a.mask[row * a.mask_stride + (tok >> 5)] >> (tok & 31)) & 1u)) x = -INFINITY;
+  return x;
+}
+
+// Position of token id in the window list that starts at `base`, or -1 when
+// the mask disallows it.
+template <int KC>
+__device__ __forceinline__ int masked_pos(const MaskedMem<KC>* mm, int id, int base) {
+  const int w = id >> 5, j = id & 31;
+  const uint32_t word = mm->mw[w];
+  if (!((word >> j) & 1u)) return -1;
+  return mm->toff[id >> 10] - base + mm->wpre[w] + __popc(word & ((1u << j) - 1u));
+}
+
+// Descending bitonic sort of S[0..n) (n <= P <= 1024, P a power of two,
+// S holds P slots) by the whole CTA.
+__device__ __forceinline__ void block_sort_desc(uint64_t* S, int n, int P) {
+  for (int i = n + threadIdx.x; i < P; i += kMThreads) S[i] = 0ull;
+  __syncthreads();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < P; i += kMThreads) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint64_t x = S[i], y = S[ixj];
+          const bool desc = (i & k) == 0;
+          if (desc ? (x < y) : (x > y)) { S[i] = y; S[ixj] = x; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float staged_value(uint32_t raw, int id) {
+  if constexpr (sizeof(T) == 4) return __uint_as_float(raw);
+  else return bf16_bits_to_f32((id & 1) ? (raw >> 16) : (raw & 0xffffu));
+}
+
+template <typename T, int KC>
+__global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_constant__ SampleArgs a) {
+  extern __shared__ __align__(128) unsigned char smem_masked[];
+  MaskedMem<KC>* mm = reinterpret_cast<MaskedMem<KC>*>(smem_masked);
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int nt = a.n_tiles;
+  const int nw = (int)((a.vocab + 31) >> 5);
+  const int KW = (nt * 32 + kMThreads - 1) / kMThreads;  // mask-word rounds: word tid + 256 k is in tile 8 k + wid
+  const uint64_t pol = policy_evict_first();
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const pm_row_params p = row_params(a, row);
+    const int mode = row_mode(p);
+    const bool needx = needs_xstats(a, p, mode);
+    const bool needy = mode == kFullDraw;
+    const bool want_max = needx || needy || mode == kCand;
+    const float inv_t = p.inv_temperature;
+    const int K = (p.top_k > 0 && p.top_k < KC) ? p.top_k : KC;
+    // 1. mask words (cut at the vocabulary), in-tile word prefixes, tile counts;
+    //    all loads first, then the scans
+    const uint32_t* mrow = a.mask + row * a.mask_stride;
+    uint32_t wr[kMaxPer * 4];
+#pragma unroll
+    for (int k = 0; k < kMaxPer * 4; ++k) {
+      const int w = tid + k * kMThreads;
+      wr[k] = (k < KW && w < nw) ? __ldcs(mrow + w) : 0u;
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxPer * 4; ++k) {
+      const int w = tid + k * kMThreads;
+      const int tile = k * kMWarps + wid;
+      if (k < KW && tile < nt) {  // warp-uniform
+        uint32_t word = wr[k];
+        if (w == nw - 1 && (a.vocab & 31)) word &= (1u << (a.vocab & 31)) - 1u;
+        mm->mw[w] = word;
+        const int pc = __popc(word);
+        const int incl = warp_incl_scan(pc);
+        mm->wpre[w] = (uint16_t)(incl - pc);
+        if (lane == 31) mm->toff[tile + 1] = incl;
+      }
+    }
+    __syncthreads();
+    if (wid == 0) {
+      int c[kMaxPer];
+      int s = 0;
+#pragma unroll
+      for (int k = 0; k < kMaxPer; ++k) {
+        const int t = lane * kMaxPer + k;
+        c[k] = t < nt ? mm->toff[t + 1] : 0;
+        s += c[k];
+      }
+      const int incl = warp_incl_scan(s);
+      int run = incl - s;
+#pragma unroll
+      for (int k = 0; k < kMaxPer; ++k) {
+        const int t = lane * kMaxPer + k;
+        run += c[k];
+        if (t < nt) mm->toff[t + 1] = run;
+      }
+      if (lane == 0) mm->toff[0] = 0;
+    }
+    __syncthreads();
+    int ncarry = 0;
+    bool dropped = false;  // a selection left keys out: the top-K may not hold every candidate
+    uint64_t tau = 0;
+    uint64_t best = 0;
+    const T* rowp = reinterpret_cast<const T*>(a.logits) + row * a.row_stride;
+    auto vf = [mm](int i) { return __uint_as_float(mm->val[i]); };
+    // 2. windows of whole tiles
+    for (int t0 = 0; t0 < nt;) {
+      const int base = mm->toff[t0];
+      int lo = t0 + 1, hi = nt;  // the last tile end whose window holds at most kWin tokens
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (mm->toff[mid] - base <= kWin) lo = mid; else hi = mid - 1;
+      }
+      const int t1 = lo;
+      const int n = mm->toff[t1] - base;
+      // gather: lane per mask word, ascending token order inside the window
+      for (int k = 0; k < KW; ++k) {
+        const int tile = k * kMWarps + wid;
+        if (tile < t0 || tile >= t1) continue;  // warp-uniform
+        const int w = tid + k * kMThreads;
+        uint32_t word = mm->mw[w];
+        int pos = mm->toff[tile] - base + mm->wpre[w];
+        const int id0 = w * 32;
+        while (word) {
+          const int id = id0 + __ffs(word) - 1;
+          word &= word - 1;
+          cp_async4(&mm->val[pos], rowp + (sizeof(T) == 4 ? id : (id & ~1)), pol);
+          mm->ids[pos] = (uint32_t)id;
+          ++pos;
+        }
+      }
+      cp_async_wait_all();
+      __syncthreads();
+      if constexpr (sizeof(T) == 2) {
+        for (int i = tid; i < n; i += kMThreads)
+          mm->val[i] = __float_as_uint(staged_value<T>(mm->val[i], (int)mm->ids[i]));
+        __syncthreads();
+      }
+      // processors on the window's overridden ids (bias first, then penalties)
+      if (a.bias_off) {
+        for (int i = a.bias_off[t0] + tid; i < a.bias_off[t1]; i += kMThreads) {
+          const int pos = masked_pos(mm, a.bias_tok[i], base);
+          if (pos >= 0) mm->val[pos] = __float_as_uint(fadd(vf(pos), a.bias_val[i]));
+        }
+        __syncthreads();
+      }
+      if (a.ovr_off) {
+        const int32_t* off = a.ovr_off + row * (int64_t)(nt + 1);
+        const int32_t* otok = a.ovr_tok + row * (int64_t)a.ovr_cap;
+        const uint32_t* oinf = a.ovr_info + row * (int64_t)a.ovr_cap;
+        for (int i = off[t0] + tid; i < off[t1]; i += kMThreads) {
+          const int pos = masked_pos(mm, otok[i], base);
+          if (pos < 0) continue;
+          const uint32_t info = oinf[i];
+          float x = vf(pos);
+          if (info & 1u) x = x < 0.0f ? fmul(x, p.repetition_penalty) : __fdiv_rn(x, p.repetition_penalty);
+          if (info & 2u) x = fsub(x, p.presence_penalty);
+          const uint32_t cnt = info >> 8;
+          if (cnt) x = fsub(x, fmul(p.frequency_penalty, (float)cnt));
+          mm->val[pos] = __float_as_uint(x);
+        }
+        __syncthreads();
+      }
+      for (int t = t0 + tid; t < t1; t += kMThreads) {
+        mm->tmx[t] = 0;
+        mm->tmy[t] = 0;
+        mm->tsx[t] = 0;
+        mm->tsy[t] = 0;
+      }
+      __syncthreads();
+      // each lane owns a contiguous run of positions (tiles are runs of positions)
+      const int rl = (n + kMThreads - 1) / kMThreads;
+      const int q0 = min(n, tid * rl), q1 = min(n, q0 + rl);
+      // exact tile statistics: maxima, then q52 sums against them
+      if (want_max) {
+        int cur = -1;
+        uint32_t mx = 0, my = 0;
+        for (int i = q0; i < q1; ++i) {
+          const float x = vf(i);
+          const int seg = (int)(mm->ids[i] >> 10);
+          if (seg != cur) {
+            if (cur >= 0) {
+              if (mx) atomicMax(&mm->tmx[cur], mx);
+              if (my) atomicMax(&mm->tmy[cur], my);
+            }
+            cur = seg;
+            mx = my = 0;
+          }
+          if (x > -INFINITY) {
+            mx = max(mx, ordkey(x));
+            if (needy) my = max(my, ordkey(fmul(x, inv_t)));
+          }
+        }
+        if (cur >= 0) {
+          if (mx) atomicMax(&mm->tmx[cur], mx);
+          if (my) atomicMax(&mm->tmy[cur], my);
+        }
+        __syncthreads();
+      }
+      if (needx || needy) {
+        int cur = -1;
+        uint64_t sx = 0, sy = 0;
+        float mxv = -INFINITY, myv = -INFINITY;
+        for (int i = q0; i < q1; ++i) {
+          const float x = vf(i);
+          const int seg = (int)(mm->ids[i] >> 10);
+          if (seg != cur) {
+            if (cur >= 0) {
+              if (sx) atomicAdd(reinterpret_cast<unsigned long long*>(&mm->tsx[cur]), (unsigned long long)sx);
+              if (sy) atomicAdd(reinterpret_cast<unsigned long long*>(&mm->tsy[cur]), (unsigned long long)sy);
+            }
+            cur = seg;
+            sx = sy = 0;
+            mxv = mm->tmx[seg] ? ord_value(mm->tmx[seg]) : -INFINITY;
+            myv = mm->tmy[seg] ? ord_value(mm->tmy[seg]) : -INFINITY;
+          }
+          if (x > -INFINITY) {
+            if (needx && mxv > -INFINITY) sx += q52(fsub(x, mxv));
+            if (needy && myv > -INFINITY) sy += q52(fsub(fmul(x, inv_t), myv));
+          }
+        }
+        if (cur >= 0) {
+          if (sx) atomicAdd(reinterpret_cast<unsigned long long*>(&mm->tsx[cur]), (unsigned long long)sx);
+          if (sy) atomicAdd(reinterpret_cast<unsigned long long*>(&mm->tsy[cur]), (unsigned long long)sy);
+        }
+        __syncthreads();
+        for (int t = t0 + tid; t < t1; t += kMThreads) {
+          TileStat st;
+          st.pad = 0;
+          if (needx) {
+            st.m = mm->tmx[t] ? ord_value(mm->tmx[t]) : -INFINITY;
+            st.s = mm->tsx[t];
+            a.statx[row * nt + t] = st;
+          }
+          if (needy) {
+            st.m = mm->tmy[t] ? ord_value(mm->tmy[t]) : -INFINITY;
+            st.s = mm->tsy[t];
+            a.staty[row * nt + t] = st;
+          }
+        }
+      }
+      // selection
+      if (mode == kGreedy) {
+        uint64_t b = 0;
+        for (int i = tid; i < n; i += kMThreads) {
+          const float x = vf(i);
+          const uint64_t k = rankkey(x, mm->ids[i]);
+          if (x > -INFINITY && k > b) b = k;  // nothing finite at all: token 0, as the streaming pass
+        }
+        b = warp_max_u64(b);
+        if (lane == 0) mm->wbest[wid] = b;
+        __syncthreads();
+#pragma unroll
+        for (int w = 0; w < kMWarps; ++w) best = mm->wbest[w] > best ? mm->wbest[w] : best;
+      } else if (mode == kCand) {
+        // v0: the K-th largest finite tile maximum of the window bounds its top-K
+        // from below (at least K tokens reach it); found by counting ranks
+        const int ntw = t1 - t0;  // <= 256 = threads
+        uint64_t tk = 0;
+        if (tid < ntw) {
+          const uint32_t v = mm->tmx[t0 + tid];
+          tk = v ? (((uint64_t)v << 32) | (uint32_t)tid) : 0ull;
+          mm->sel[tid] = tk;
+        }
+        if (tid == 0) { mm->v0 = -INFINITY; mm->nsel = 0; }
+        __syncthreads();
+        if (tk) {
+          int rank = 0;
+          for (int t = 0; t < ntw; ++t) rank += mm->sel[t] > tk;
+          if (rank == K - 1) mm->v0 = ord_value((uint32_t)(tk >> 32));
+        }
+        __syncthreads();
+        const float v0 = mm->v0;
+        // keys of the window that can still enter the top-K
+        for (int i = q0; i < q1; ++i) {
+          const float x = vf(i);
+          if (!(x > -INFINITY) || x < v0) continue;
+          const uint64_t k = rankkey(x, mm->ids[i]);
+          if (k <= tau) continue;
+          const int at = atomicAdd(&mm->nsel, 1);
+          if (at < kSel) mm->sel[at] = k;
+        }
+        __syncthreads();
+        const int ns = mm->nsel;
+        if (ns <= kSel) {
+          for (int i = tid; i < ncarry; i += kMThreads) mm->sel[ns + i] = mm->carry[i];
+          __syncthreads();
+          const int total = ns + ncarry;
+          dropped |= total > K;
+          if (total <= 512) {
+            // rank by counting: the K largest land sorted in the carry
+            for (int i = tid; i < total; i += kMThreads) {
+              const uint64_t k = mm->sel[i];
+              int rank = 0;
+              for (int j = 0; j < total; ++j) rank += mm->sel[j] > k;
+              if (rank < K) mm->carry[rank] = k;
+            }
+            ncarry = total < K ? total : K;
+          } else {
+            ncarry = block_topk_sorted(mm->sel, total, K, mm->carry, KC, mm->hist, mm->scal);
+          }
+        } else {
+          // more than kSel keys qualify: radix-select the K-th key over the
+          // window (keys recomputed on the fly) and the carry, then keep the K
+          dropped = true;
+          uint64_t prefix = 0;
+          int need = K;
+          for (int shift = 56; shift >= 0; shift -= 8) {
+            for (int i = tid; i < 256; i += kMThreads) mm->hist[i] = 0;
+            __syncthreads();
+            const int hs = shift + 8;
+            for (int i = tid; i < n + ncarry; i += kMThreads) {
+              uint64_t k;
+              if (i < n) {
+                const float x = vf(i);
+                if (!(x > -INFINITY) || x < v0) continue;
+                k = rankkey(x, mm->ids[i]);
+                if (k <= tau) continue;
+              } else {
+                k = mm->carry[i - n];
+              }
+              if (hs < 64 && (k >> hs) != (prefix >> hs)) continue;
+              atomicAdd(&mm->hist[(k >> shift) & 255], 1u);
+            }
+            __syncthreads();
+            if (wid == 0) {
+              int above, in_bin;
+              const int d = warp_find_digit(mm->hist, need, &above, &in_bin);
+              if (lane == 0) { mm->scal[0] = d; mm->scal[1] = above; mm->scal[2] = in_bin; }
+            }
+            __syncthreads();
+            need -= mm->scal[1];
+            prefix |= (uint64_t)(mm->scal[0] & 255) << shift;
+            const bool whole = mm->scal[2] == need;
+            __syncthreads();
+            if (whole) break;  // every key of the bin is in: keys >= prefix are exactly the top K
+          }
+          if (tid == 0) mm->nsel = 0;
+          __syncthreads();
+          for (int i = tid; i < n + ncarry; i += kMThreads) {
+            uint64_t k;
+            if (i < n) {
+              const float x = vf(i);
+              if (!(x > -INFINITY) || x < v0) continue;
+              k = rankkey(x, mm->ids[i]);
+              if (k <= tau) continue;
+            } else {
+              k = mm->carry[i - n];
+            }
+            if (k >= prefix) mm->sel[atomicAdd(&mm->nsel, 1)] = k;
+          }
+          __syncthreads();
+          int P = 1;
+          while (P < K) P <<= 1;
+          block_sort_desc(mm->sel, K, P);
+          for (int i = tid; i < K; i += kMThreads) mm->carry[i] = mm->sel[i];
+          ncarry = K;
+        }
+        __syncthreads();
+        tau = ncarry == K ? mm->carry[K - 1] : 0ull;
+      }
+      __syncthreads();
+      t0 = t1;
+    }
+    // 3. the draw: log-sum-exp (warp 0) and the carried keys' Gumbel scores
+    //    (every other thread) side by side, then filters and draw (warp 0)
+    if (wid == 0 && needx) {
+      LaneTiles lt;
+      int P = 32;
+      while (P < nt) P <<= 1;
+      lt.per = P >> 5;
+      lt.nt = nt;
+#pragma unroll
+      for (int i = 0; i < kMaxPer; ++i) {
+        const int t = lane * lt.per + i;
+        const bool ok = i < lt.per && t < nt && mm->tmx[t] != 0;
+        lt.m[i] = ok ? ord_value(mm->tmx[t]) : -INFINITY;
+        lt.s[i] = ok ? mm->tsx[t] : 0ull;
+      }
+      const float cc = combine_lane_tiles(lt, lane_tiles_max(lt));
+      if (lane == 0) mm->lse = cc;
+    }
+    if (mode == kCand)
+      for (int r = tid - 32; r >= 0 && r < ncarry; r += kMThreads - 32)
+        mm->score[r] = fadd(fmul(key_value(mm->carry[r]), inv_t), row_gumbel(a, row, key_index(mm->carry[r])));
+    __syncthreads();
+    if (wid == 0) {
+      const float c = needx ? mm->lse : __int_as_float(0x7fc00000);
+      int tok = 0, ns = 0;
+      float x_tok = -INFINITY;
+      if (mode == kGreedy) {
+        if (best) {
+          tok = (int)key_index(best);
+          x_tok = key_value(best);
+        }
+      } else if (mode == kCand) {
+        tok = warp_filter_draw(a, p, row, mm->carry, ncarry, !dropped, c, &ns, mm->score);
+        if (tok >= 0) {
+          float fx = -INFINITY;
+          for (int r = lane; r < ncarry; r += 32)
+            if ((int)key_index(mm->carry[r]) == tok) fx = key_value(mm->carry[r]);
+          x_tok = warp_max(fx);
+          if (a.surv_ids && lane == 0) write_survivors(a, p, row, mm->carry, ns);
+        }
+      } else {
+        tok = warp_full_draw<T>(a, p, row, &x_tok);  // reads the y statistics this CTA wrote
+      }
+      if (lane == 0) write_row(a, row, mode, tok, x_tok, c, ns);
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace pm

@@ -585,6 +585,8 @@ __global__ void k_bias_offsets(const int32_t* tok, int n, int n_tiles, int32_t* 
 
 }  // namespace pm
 
+#include "pm_masked.cuh"
+#include "pm_wide.cuh"
 #include "pm_verify_impl.cuh"
 
 // ============================================================================
@@ -842,6 +844,59 @@ int launch_stream_any(int dtype, int KC, const pm::SampleArgs& a, bool cand_rows
   return bf ? launch_stream<__nv_bfloat16, 256>(a, cand_rows, st) : launch_stream<float, 256>(a, cand_rows, st);
 }
 
+// Masked rows go through the one-CTA-per-row gather pass when their logits
+// can be fetched as aligned 4-byte words (always for fp32; bf16 rows need an
+// even stride and a 4-byte aligned base).
+bool masked_path(const pm_rows* r) {
+  if (!r->mask) return false;
+  if (r->dtype == PM_DTYPE_F32) return true;
+  return ((uintptr_t)r->logits % 4 == 0) && (r->row_stride % 2 == 0);
+}
+
+template <typename T, int KC>
+int launch_masked(const pm::SampleArgs& a, cudaStream_t st) {
+  const size_t smem = sizeof(pm::MaskedMem<KC>);
+  static std::once_flag once;
+  std::call_once(once, [smem] {
+    cudaFuncSetAttribute(pm::k_sample_masked<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  });
+  int64_t grid = a.rows;
+  if (grid > (int64_t)num_sms() * 2) grid = (int64_t)num_sms() * 2;
+  pm::k_sample_masked<T, KC><<<(unsigned)grid, pm::kMThreads, smem, st>>>(a);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PM_OK : cuda_fail(e);
+}
+
+template <typename T>
+int launch_wide(const pm::SampleArgs& a, cudaStream_t st) {
+  const size_t smem = sizeof(pm::WideMem);
+  static std::once_flag once;
+  std::call_once(once, [smem] {
+    cudaFuncSetAttribute(pm::k_row_wide<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  });
+  int64_t grid = a.rows;
+  if (grid > (int64_t)num_sms() * 2) grid = (int64_t)num_sms() * 2;
+  pm::k_row_wide<T><<<(unsigned)grid, pm::kWThreads, smem, st>>>(a);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PM_OK : cuda_fail(e);
+}
+
+// The sampling pass over prepared arguments: gather pass for masked rows,
+// streaming + merge otherwise; then, when some row has an unbounded filter,
+// the exact finish of rows whose survivors outran the candidates.
+int launch_rows(const pm_rows* r, int KC, const pm::SampleArgs& a, cudaStream_t st) {
+  const bool bf = r->dtype == PM_DTYPE_BF16;
+  int rc;
+  if (masked_path(r)) {
+    if (KC == 64) rc = bf ? launch_masked<__nv_bfloat16, 64>(a, st) : launch_masked<float, 64>(a, st);
+    else rc = bf ? launch_masked<__nv_bfloat16, 256>(a, st) : launch_masked<float, 256>(a, st);
+  } else {
+    rc = launch_stream_any(r->dtype, KC, a, has_cand_rows(r), st);
+  }
+  if (rc || !(r->flags_any & PM_F_UNBOUNDED)) return rc;
+  return bf ? launch_wide<__nv_bfloat16>(a, st) : launch_wide<float>(a, st);
+}
+
 int check_noise(const pm_rows* rows, const pm_noise* noise) {
   if (!noise) return PM_ERR_ARG;
   if (noise->mode != PM_NOISE_PHILOX && noise->mode != PM_NOISE_INJECTED) return PM_ERR_ARG;
@@ -980,7 +1035,7 @@ int pm_sample_rows(const pm_rows* rows, const pm_noise* noise, const pm_sample_o
   a.n_surv = out->n_surv;
   a.surv_cap = out->surv_cap;
   a.want_lse = out->lse != nullptr || out->token_logprob != nullptr;
-  return launch_stream_any(rows->dtype, L.KC, a, has_cand_rows(rows), st);
+  return launch_rows(rows, L.KC, a, st);
 }
 
 size_t pm_processors_workspace_bytes(const pm_rows* rows) { return pm_sample_workspace_bytes(rows); }
@@ -1082,7 +1137,7 @@ int pm_verify(const pm_rows* rows, const pm_noise* noise, const pm_verify_args* 
     a.surv_probs = reinterpret_cast<float*>(ws + V.sprobs);
     a.surv_cap = V.scap;
   }
-  rc = launch_stream_any(rows->dtype, V.L.KC, a, has_cand_rows(rows), st);
+  rc = launch_rows(rows, V.L.KC, a, st);
   if (rc) return rc;
   pm::VerifyK vk;
   memset(&vk, 0, sizeof(vk));

@@ -56,36 +56,6 @@ __device__ __forceinline__ uint64_t residual_q52(float p, float q) {
   return r > 0.0f ? __float2ull_rz(fmul(r, 0x1p52f)) : 0ull;
 }
 
-// The processed logit of one token of a row (bias, penalties, mask): the
-// single-token form of process_tile.
-__device__ float processed_value(const SampleArgs& a, int dtype, const pm_row_params& p, int64_t row, int tok) {
-  float x;
-  if (dtype == PM_DTYPE_F32) x = reinterpret_cast<const float*>(a.logits)[row * a.row_stride + tok];
-  else x = bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(a.logits)[row * a.row_stride + tok]);
-  const int tile = tok / kTile;
-  if (a.bias_off)
-    for (int i = a.bias_off[tile]; i < a.bias_off[tile + 1]; ++i)
-      if (a.bias_tok[i] == tok) x = fadd(x, a.bias_val[i]);
-  if (a.ovr_off) {
-    const int32_t* off = a.ovr_off + row * (int64_t)(a.n_tiles + 1) + tile;
-    const int32_t* otok = a.ovr_tok + row * (int64_t)a.ovr_cap;
-    int lo = off[0], hi = off[1];
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (otok[mid] < tok) lo = mid + 1; else hi = mid;
-    }
-    if (lo < off[1] && otok[lo] == tok) {
-      const uint32_t info = a.ovr_info[row * (int64_t)a.ovr_cap + lo];
-      if (info & 1u) x = x < 0.0f ? fmul(x, p.repetition_penalty) : __fdiv_rn(x, p.repetition_penalty);
-      if (info & 2u) x = fsub(x, p.presence_penalty);
-      const uint32_t cnt = info >> 8;
-      if (cnt) x = fsub(x, fmul(p.frequency_penalty, (float)cnt));
-    }
-  }
-  if (a.mask && !((a.mask[row * a.mask_stride + (tok >> 5)] >> (tok & 31)) & 1u)) x = -INFINITY;
-  return x;
-}
-
 __device__ __forceinline__ double accept_uniform(const SampleArgs& a, const VerifyK& v, int64_t b, int i,
                                                  int64_t row) {
   if (v.u_accept) return v.u_accept[b * v.k + i];
@@ -103,7 +73,7 @@ template <int KC>
 __device__ int survivor_residual(const SampleArgs& a, const VerifyK& v, int64_t b, int64_t row, int64_t drow,
                                  float cd, uint64_t* key, uint64_t* q) {
   const int lane = threadIdx.x & 31;
-  const int n = ld_cg(&v.ns[row]);
+  const int n = min(ld_cg(&v.ns[row]), v.scap);
   uint64_t R = 0;
   for (int r = lane; r < n; r += 32) {
     const int id = ld_cg(&v.sids[row * v.scap + r]);
@@ -171,6 +141,7 @@ __global__ void __launch_bounds__(256) k_verify_accept(const __grid_constant__ S
     int i = 0;
     int final_tok = 0;
     bool pend = false;
+    bool wide = false;
     for (; i < v.k; ++i) {
       const int64_t row = base + i;
       const int64_t drow = b * v.k + i;
@@ -184,6 +155,10 @@ __global__ void __launch_bounds__(256) k_verify_accept(const __grid_constant__ S
         p_d = ld_cg(&v.rtok[row]) == d ? 1.0f : 0.0f;
       } else if (mode == kCand) {
         const int n = ld_cg(&v.ns[row]);
+        if (n > v.scap) {  // survivors beyond the candidate lists: this request cannot be judged exactly
+          wide = true;
+          break;
+        }
         float f = 0.0f;
         for (int r = lane; r < n; r += 32)
           if (ld_cg(&v.sids[row * v.scap + r]) == d) f = ld_cg(&v.sprobs[row * v.scap + r]);
@@ -206,6 +181,12 @@ __global__ void __launch_bounds__(256) k_verify_accept(const __grid_constant__ S
         pend = true;  // whole vocabulary: k_verify_residual draws it
       }
       break;
+    }
+    if (wide) {
+      for (int r = lane; r < K1; r += 32) out[r] = -1;
+      if (lane == 0) { v.n_acc[b] = -1; v.pending[b] = -1; }
+      __syncwarp();
+      continue;
     }
     if (i == v.k) final_tok = ld_cg(&v.rtok[base + v.k]);  // every draft accepted: the bonus token
     for (int r = lane; r < K1; r += 32)

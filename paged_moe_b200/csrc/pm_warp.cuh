@@ -228,7 +228,7 @@ __device__ __forceinline__ uint64_t row_u53(const SampleArgs& a, int64_t row, in
 // Returns the token, or -1 when the survivors reach past the candidates (the
 // row is then flagged; only possible when top_k is off).  *n_out = survivors.
 __device__ int warp_filter_draw(const SampleArgs& a, const pm_row_params& p, int64_t row, const uint64_t* S,
-                                int m, bool complete, float c, int* n_out) {
+                                int m, bool complete, float c, int* n_out, const float* scores = nullptr) {
   const int lane = threadIdx.x & 31;
   *n_out = 0;
   if (m == 0) return 0;
@@ -275,7 +275,7 @@ __device__ int warp_filter_draw(const SampleArgs& a, const pm_row_params& p, int
   int bid = -1;
   for (int r = lane; r < cnt; r += 32) {
     const uint32_t id = key_index(S[r]);
-    const float sc = fadd(fmul(key_value(S[r]), p.inv_temperature), row_gumbel(a, row, id));
+    const float sc = scores ? scores[r] : fadd(fmul(key_value(S[r]), p.inv_temperature), row_gumbel(a, row, id));
     if (bid < 0 || sc > bs || (sc == bs && (int)id < bid)) { bs = sc; bid = (int)id; }
   }
 #pragma unroll
@@ -517,7 +517,7 @@ __device__ __noinline__ int warp_row_merge(const SampleArgs& a, int64_t row, int
     if (cd.cnt > K) cand_compact<CAP>(cbuf, hist, cd, K);
     warp_sort_desc(cbuf, cd.cnt);
     int ns = 0;
-    tok = warp_filter_draw(a, p, row, cbuf, cd.cnt, !trimmed_any, c, &ns);
+    tok = warp_filter_draw(a, p, row, cbuf, cd.cnt, !(trimmed_any || cd.trimmed), c, &ns);
     *n_surv_out = ns;
     if (tok >= 0) {
       for (int r = 0; r < cd.cnt; ++r)
