@@ -143,8 +143,8 @@ typedef struct pm_sample_out {
     int32_t surv_cap;
 } pm_sample_out;
 
-/* Workspace bytes pm_sample_rows needs for these rows.  The workspace must be
- * zero-filled before its first use; every call leaves it ready for the next. */
+/* Workspace bytes pm_sample_rows needs for these rows.  Nothing in the
+ * workspace needs to start at zero. */
 PM_API size_t pm_sample_workspace_bytes(const pm_rows *rows);
 
 /* One fused pass: processors, row log-sum-exp, top-k / top-p / min-p,
@@ -192,6 +192,33 @@ typedef struct pm_verify_args {
 PM_API size_t pm_verify_workspace_bytes(const pm_rows *rows, const pm_verify_args *v);
 PM_API int pm_verify(const pm_rows *rows, const pm_noise *noise, const pm_verify_args *v, void *workspace,
                      size_t workspace_bytes, void *stream);
+
+/* Vocabulary-sharded sampling (no reference code: the reference runs on one
+ * device).  A tensor-parallel LM head leaves shard i with the contiguous ids
+ * [i * shard_width, min((i + 1) * shard_width, vocab_total)) of every row;
+ * every shard but the last must be a whole number of 1024-token tiles.  Each
+ * shard calls pm_shard_summarize on its slice (rows->vocab = its width, the
+ * mask its slice of words, bias ids shifted to the slice; history ids stay
+ * global), the caller all-gathers the summaries in shard order (one NCCL
+ * all-gather of pm_shard_summary_bytes per shard), and pm_shard_merge gives
+ * every rank the row's tokens -- the same tokens, log-sum-exp and survivor
+ * lists pm_sample_rows gives on the unsharded rows.  Rows whose unbounded
+ * top-p / min-p keeps more than 256 tokens are flagged (status 1, token -1). */
+typedef struct pm_shard {
+    int32_t shard_index;
+    int32_t n_shards;
+    int64_t vocab_total;
+    int64_t shard_width;         /* ids per shard (the last may hold fewer) */
+} pm_shard;
+
+PM_API size_t pm_shard_summary_bytes(const pm_rows *rows, const pm_shard *shard);
+PM_API int pm_shard_summarize(const pm_rows *rows, const pm_shard *shard, const pm_noise *noise, void *summary,
+                              void *workspace, size_t workspace_bytes, void *stream);
+/* rows: the sampler settings (params, flags_any, top_k_max, rows) with
+ * vocab = vocab_total; logits are not read.  summaries: [n_shards] summaries
+ * back to back.  workspace: at least 4 * rows bytes (row status). */
+PM_API int pm_shard_merge(const pm_rows *rows, const pm_shard *shard, const pm_noise *noise, const void *summaries,
+                          const pm_sample_out *out, void *workspace, size_t workspace_bytes, void *stream);
 
 /* pm_sample_rows on scratch owned by the library (no counterpart in the
  * reference, which runs on MLX's allocator): for callers that cannot hand

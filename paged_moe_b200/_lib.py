@@ -95,7 +95,7 @@ class VerifyArgs(C.Structure):
 class ShardArgs(C.Structure):
     _fields_ = [
         ("shard_index", C.c_int32), ("n_shards", C.c_int32), ("vocab_total", C.c_int64),
-        ("shard_offset", C.c_int64), ("cand_k", C.c_int32),
+        ("shard_width", C.c_int64),
     ]
 
 
@@ -113,7 +113,7 @@ SIGNATURES = {
     "pm_verify_workspace_bytes": (C.c_size_t, [_P, _P]),
     "pm_verify": (C.c_int, [_P, _P, _P, _P, C.c_size_t, _P]),
     "pm_shard_summary_bytes": (C.c_size_t, [_P, _P]),
-    "pm_shard_summarize": (C.c_int, [_P, _P, _P, _P, C.c_size_t, _P]),
+    "pm_shard_summarize": (C.c_int, [_P, _P, _P, _P, _P, C.c_size_t, _P]),
     "pm_shard_merge": (C.c_int, [_P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
 }
 

@@ -27,6 +27,7 @@ struct PrepArgs {
   int32_t params_per_row;
   int64_t rows;
   int64_t vocab;
+  int64_t id_base;    // first token id of these rows' vocabulary slice (a vocabulary shard), else 0
   int32_t n_tiles;
   int32_t cap;        // entries per row in the output lists (power of two)
   int32_t* ovr_tok;   // [rows, cap]
@@ -72,8 +73,9 @@ __global__ void __launch_bounds__(1024) k_prep_overrides(PrepArgs a) {
     uint64_t k = ~0ull;
     if (i < n) {
       const int pos = s + i;
-      const int tok = pos < Hb ? a.hist[b * a.hist_stride + pos] : a.feed[b * a.feed_group + (pos - Hb)];
-      if (tok >= 0 && (int64_t)tok < a.vocab) k = ((uint64_t)(uint32_t)tok << 32) | (uint32_t)pos;
+      const int64_t tok =
+          (int64_t)(pos < Hb ? a.hist[b * a.hist_stride + pos] : a.feed[b * a.feed_group + (pos - Hb)]) - a.id_base;
+      if (tok >= 0 && tok < a.vocab) k = ((uint64_t)(uint32_t)tok << 32) | (uint32_t)pos;
     }
     keys[i] = k;
   }

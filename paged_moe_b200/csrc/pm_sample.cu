@@ -588,6 +588,7 @@ __global__ void k_bias_offsets(const int32_t* tok, int n, int n_tiles, int32_t* 
 #include "pm_masked.cuh"
 #include "pm_wide.cuh"
 #include "pm_verify_impl.cuh"
+#include "pm_shard_impl.cuh"
 
 // ============================================================================
 // host side
@@ -715,7 +716,8 @@ int check_rows(const pm_rows* r) {
 }
 
 // prep kernels shared by every entry point; fills the processor fields of a
-int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::SampleArgs& a, cudaStream_t st) {
+int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::SampleArgs& a, cudaStream_t st,
+                int64_t id_base = 0) {
   a.logits = r->logits;
   a.rows = r->rows;
   a.vocab = r->vocab;
@@ -760,6 +762,7 @@ int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::Sample
     pa.params_per_row = r->params_per_row;
     pa.rows = r->rows;
     pa.vocab = r->vocab;
+    pa.id_base = id_base;
     pa.n_tiles = L.n_tiles;
     pa.cap = L.ovr_cap;
     pa.ovr_tok = reinterpret_cast<int32_t*>(ws + L.ovr_tok);
@@ -796,7 +799,7 @@ bool has_cand_rows(const pm_rows* r) {
 }
 
 template <typename T, int KC>
-int launch_stream(const pm::SampleArgs& a, bool cand_rows, cudaStream_t st) {
+int launch_stream(const pm::SampleArgs& a, bool cand_rows, cudaStream_t st, bool merge = true) {
   stream_occupancy<T, KC>();
   const size_t smem = sizeof(pm::StreamMem<KC>) * pm::kWarpsS;
   const int64_t grid = (a.n_warps + pm::kWarpsS - 1) / pm::kWarpsS;
@@ -809,6 +812,7 @@ int launch_stream(const pm::SampleArgs& a, bool cand_rows, cudaStream_t st) {
   pm::k_sample_stream<T, KC><<<(unsigned)grid, pm::kThreadsS, smem, st>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
+  if (!merge) return PM_OK;
   // the row merges: one warp per row, chained by programmatic dependent launch
   constexpr int kMergeWarps = 8;
   const size_t msmem = (sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * kMergeWarps;
@@ -1171,6 +1175,210 @@ int pm_verify(const pm_rows* rows, const pm_noise* noise, const pm_verify_args* 
     if (e != cudaSuccess) return cuda_fail(e);
   }
   return PM_OK;
+}
+
+}  // extern "C"
+
+// ============================================================================
+// vocabulary-sharded sampling
+// ============================================================================
+namespace {
+
+int shard_layout(const pm_rows* r, const pm_shard* sh, pm::ShardLayout* S) {
+  if (!r || !sh) return PM_ERR_ARG;
+  if (sh->n_shards < 1 || sh->shard_index < 0 || sh->shard_index >= sh->n_shards) return PM_ERR_ARG;
+  if (sh->shard_width <= 0 || sh->vocab_total <= 0) return PM_ERR_ARG;
+  if (sh->n_shards > 1 && sh->shard_width % pm::kTile) return PM_ERR_ARG;
+  const int64_t last = sh->vocab_total - (int64_t)(sh->n_shards - 1) * sh->shard_width;
+  if (last <= 0 || last > sh->shard_width) return PM_ERR_ARG;
+  if (sh->vocab_total > (int64_t)32 * pm::kMaxPer * pm::kTile) return PM_ERR_UNSUPPORTED;
+  int need = r->top_k_max > 0 ? r->top_k_max : 0;
+  if (r->flags_any & PM_F_UNBOUNDED) need = need > 256 ? need : 256;
+  if (need > 256) return PM_ERR_UNSUPPORTED;
+  S->cand_k = need <= 64 ? 64 : 256;
+  S->nts = (int)((sh->shard_width + pm::kTile - 1) / pm::kTile);
+  S->full = (r->flags_any & PM_F_FULL) != 0;
+  size_t o = 16;
+  S->keys = o;
+  o += sizeof(uint64_t) * S->cand_k;
+  S->xst = o;
+  o += sizeof(pm::TileStat) * S->nts;
+  S->yst = S->ttok = S->tx = o;
+  if (S->full) {
+    S->yst = o;
+    o += sizeof(pm::TileStat) * S->nts;
+    S->ttok = o;
+    o += sizeof(int32_t) * S->nts;
+    S->tx = o;
+    o += sizeof(float) * S->nts;
+  }
+  S->row_bytes = align_up(o, 16);
+  return PM_OK;
+}
+
+int64_t shard_vocab(const pm_shard* sh) {
+  const int64_t last = sh->vocab_total - (int64_t)(sh->n_shards - 1) * sh->shard_width;
+  return sh->shard_index == sh->n_shards - 1 ? last : sh->shard_width;
+}
+
+template <typename T, int KC>
+int launch_shard_pack(const pm::SampleArgs& a, const pm::ShardK& sk, cudaStream_t st) {
+  constexpr int kWarpsP = 8;
+  const size_t smem = (sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * kWarpsP;
+  static std::once_flag once;
+  std::call_once(once, [smem] {
+    cudaFuncSetAttribute(pm::k_shard_pack<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  });
+  int64_t grid = (a.rows + kWarpsP - 1) / kWarpsP;
+  if (grid > (int64_t)num_sms() * 8) grid = (int64_t)num_sms() * 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(32 * kWarpsP);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, pm::k_shard_pack<T, KC>, a, sk);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    pm::k_shard_pack<T, KC><<<(unsigned)grid, 32 * kWarpsP, smem, st>>>(a, sk);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (sk.full) {
+    int64_t g2 = (a.rows * a.n_tiles + 7) / 8;
+    if (g2 > (int64_t)num_sms() * 16) g2 = (int64_t)num_sms() * 16;
+    pm::k_shard_tiles<T><<<(unsigned)g2, 256, 0, st>>>(a, sk);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
+  return PM_OK;
+}
+
+template <typename T, int KC>
+int shard_stream_and_pack(const pm::SampleArgs& a, const pm::ShardK& sk, bool cand_rows, cudaStream_t st) {
+  const int rc = launch_stream<T, KC>(a, cand_rows, st, false);
+  if (rc) return rc;
+  return launch_shard_pack<T, KC>(a, sk, st);
+}
+
+template <int KC>
+int launch_shard_merge(const pm::SampleArgs& a, const pm::MergeK& m, cudaStream_t st) {
+  constexpr int kWarpsM = 8;
+  const size_t smem = (sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * kWarpsM;
+  static std::once_flag once;
+  std::call_once(once, [smem] {
+    cudaFuncSetAttribute(pm::k_shard_merge<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  });
+  int64_t grid = (a.rows + kWarpsM - 1) / kWarpsM;
+  if (grid > (int64_t)num_sms() * 8) grid = (int64_t)num_sms() * 8;
+  pm::k_shard_merge<KC><<<(unsigned)grid, 32 * kWarpsM, smem, st>>>(a, m);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PM_OK : cuda_fail(e);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t pm_shard_summary_bytes(const pm_rows* rows, const pm_shard* shard) {
+  pm::ShardLayout S;
+  if (!rows || rows->rows < 0 || shard_layout(rows, shard, &S) != PM_OK) return 0;
+  return S.row_bytes * (size_t)rows->rows;
+}
+
+int pm_shard_summarize(const pm_rows* rows, const pm_shard* shard, const pm_noise* noise, void* summary,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_rows(rows);
+  if (rc) return rc;
+  pm::ShardLayout S;
+  rc = shard_layout(rows, shard, &S);
+  if (rc) return rc;
+  if (rows->vocab != shard_vocab(shard)) return PM_ERR_ARG;
+  if (!summary || !workspace) return PM_ERR_ARG;
+  rc = check_noise(rows, noise);
+  if (rc) return rc;
+  Layout L;
+  rc = plan(rows, &L);
+  if (rc) return rc;
+  if (workspace_bytes < L.total) return PM_ERR_WORKSPACE;
+  if (rows->rows == 0) return PM_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  unsigned char* ws = reinterpret_cast<unsigned char*>(workspace);
+  const int64_t id_base = (int64_t)shard->shard_index * shard->shard_width;
+  pm::SampleArgs a;
+  memset(&a, 0, sizeof(a));
+  rc = launch_prep(rows, L, ws, a, st, id_base);
+  if (rc) return rc;
+  set_noise(noise, a);
+  a.want_lse = true;  // the merge may ask for the log-sum-exp: every row records its x statistics
+  pm::ShardK sk;
+  sk.rec = reinterpret_cast<unsigned char*>(summary);
+  sk.row_bytes = (int64_t)S.row_bytes;
+  sk.keys = (int64_t)S.keys;
+  sk.xst = (int64_t)S.xst;
+  sk.yst = (int64_t)S.yst;
+  sk.ttok = (int64_t)S.ttok;
+  sk.tx = (int64_t)S.tx;
+  sk.cand_k = S.cand_k;
+  sk.id_base = (uint32_t)id_base;
+  sk.full = S.full;
+  const bool bf = rows->dtype == PM_DTYPE_BF16;
+  const bool cand = has_cand_rows(rows);
+  if (L.KC == 64) rc = bf ? shard_stream_and_pack<__nv_bfloat16, 64>(a, sk, cand, st)
+                          : shard_stream_and_pack<float, 64>(a, sk, cand, st);
+  else rc = bf ? shard_stream_and_pack<__nv_bfloat16, 256>(a, sk, cand, st)
+               : shard_stream_and_pack<float, 256>(a, sk, cand, st);
+  return rc;
+}
+
+int pm_shard_merge(const pm_rows* rows, const pm_shard* shard, const pm_noise* noise, const void* summaries,
+                   const pm_sample_out* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!rows || !rows->params || rows->rows < 0 || !summaries || !out || !out->tokens || !workspace) return PM_ERR_ARG;
+  if (rows->vocab != (shard ? shard->vocab_total : -1)) return PM_ERR_ARG;
+  if (out->surv_ids && (!out->surv_probs || !out->n_surv || out->surv_cap <= 0)) return PM_ERR_ARG;
+  pm::ShardLayout S;
+  int rc = shard_layout(rows, shard, &S);
+  if (rc) return rc;
+  rc = check_noise(rows, noise);
+  if (rc) return rc;
+  if (workspace_bytes < sizeof(int32_t) * (size_t)rows->rows) return PM_ERR_WORKSPACE;
+  if (rows->rows == 0) return PM_OK;
+  pm::SampleArgs a;
+  memset(&a, 0, sizeof(a));
+  a.rows = rows->rows;
+  a.vocab = rows->vocab;
+  a.params = rows->params;
+  a.params_per_row = rows->params_per_row;
+  set_noise(noise, a);
+  a.tokens = out->tokens;
+  a.lse_out = out->lse;
+  a.tok_logprob = out->token_logprob;
+  a.surv_ids = out->surv_ids;
+  a.surv_probs = out->surv_probs;
+  a.n_surv = out->n_surv;
+  a.surv_cap = out->surv_cap;
+  a.want_lse = out->lse != nullptr || out->token_logprob != nullptr;
+  a.status = reinterpret_cast<int32_t*>(workspace);
+  pm::MergeK m;
+  m.recs = reinterpret_cast<const unsigned char*>(summaries);
+  m.row_bytes = (int64_t)S.row_bytes;
+  m.shard_bytes = (int64_t)S.row_bytes * rows->rows;
+  m.keys = (int64_t)S.keys;
+  m.xst = (int64_t)S.xst;
+  m.yst = (int64_t)S.yst;
+  m.ttok = (int64_t)S.ttok;
+  m.tx = (int64_t)S.tx;
+  m.n_shards = shard->n_shards;
+  m.nts = S.nts;
+  m.nt = (int)((rows->vocab + pm::kTile - 1) / pm::kTile);
+  m.cand_k = S.cand_k;
+  a.n_tiles = m.nt;
+  return S.cand_k == 64 ? launch_shard_merge<64>(a, m, reinterpret_cast<cudaStream_t>(stream))
+                        : launch_shard_merge<256>(a, m, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -22,7 +22,8 @@ def declared():
 def test_header_declares_the_boundary():
     names = declared()
     for n in ("pm_sample_rows", "pm_sample_workspace_bytes", "pm_apply_processors", "pm_logprobs", "pm_verify",
-              "pm_verify_workspace_bytes", "pm_version"):
+              "pm_verify_workspace_bytes", "pm_shard_summarize", "pm_shard_merge", "pm_shard_summary_bytes",
+              "pm_sample_rows_static", "pm_version"):
         assert n in names, n
 
 
@@ -137,3 +138,28 @@ def test_verify_workspace_query():
     assert lib.pm_verify_workspace_bytes(C.byref(r), C.byref(_vargs(n_draft=2))) == 0
     assert lib.pm_verify(C.byref(r), C.byref(L.Noise()), C.byref(_vargs()), 0x5000, match - 1, None) == \
         L.PM_ERR_WORKSPACE
+
+
+def _shard(i=0, n=8, V=262144, w=32768):
+    s = L.ShardArgs()
+    s.shard_index, s.n_shards, s.vocab_total, s.shard_width = i, n, V, w
+    return s
+
+
+def test_shard_layout_and_checks():
+    lib = L.load()
+    r = _rows(vocab=32768, row_stride=32768, top_k_max=64, flags_any=L.PM_F_TOP_P)
+    assert lib.pm_shard_summary_bytes(C.byref(r), C.byref(_shard())) > 0
+    assert lib.pm_shard_summary_bytes(C.byref(r), C.byref(_shard(w=30000))) == 0  # not whole tiles
+    assert lib.pm_shard_summary_bytes(C.byref(r), C.byref(_shard(i=8))) == 0
+    assert lib.pm_shard_summary_bytes(C.byref(r), C.byref(_shard(V=300000, w=37888))) == 0
+    nz = L.Noise()
+    # a slice of the wrong width is refused before any launch
+    r2 = _rows(vocab=1000, row_stride=1000)
+    assert lib.pm_shard_summarize(C.byref(r2), C.byref(_shard()), C.byref(nz), 0x9000, 0x5000, 1 << 30, None) == \
+        L.PM_ERR_ARG
+    out = L.SampleOut()
+    out.tokens = 0x4000
+    r3 = _rows(vocab=262144, row_stride=262144)
+    assert lib.pm_shard_merge(C.byref(r3), C.byref(_shard()), C.byref(nz), 0x9000, C.byref(out), 0x5000, 3,
+                              None) == L.PM_ERR_WORKSPACE
