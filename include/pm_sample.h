@@ -220,6 +220,19 @@ PM_API int pm_shard_summarize(const pm_rows *rows, const pm_shard *shard, const 
 PM_API int pm_shard_merge(const pm_rows *rows, const pm_shard *shard, const pm_noise *noise, const void *summaries,
                           const pm_sample_out *out, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Batched n-gram drafts: replaces lookup_decode.draft_ngram
+ * (pagedmoe/lookup_decode.py:184-221), which scans one request's context per
+ * call in Python.  For every request, up to k tokens that followed the
+ * latest earlier occurrence of the longest suffix (n_max down to n_min
+ * tokens; reference defaults 8 and 3, config.py:1288-1289) -- the latest
+ * occurrence with k tokens after it, else the one with the most.  hist:
+ * [requests, hist_stride] device ids with optional lengths; drafts:
+ * [requests, k] (-1 after draft_len); match_n: the n that matched (0: none),
+ * may be NULL.  n_max <= 32. */
+PM_API int pm_draft_ngram(const int32_t *hist, const int32_t *hist_len, int64_t hist_stride, int64_t requests,
+                          int32_t k, int32_t n_min, int32_t n_max, int32_t *drafts, int32_t *draft_len,
+                          int32_t *match_n, void *stream);
+
 /* pm_sample_rows on scratch owned by the library (no counterpart in the
  * reference, which runs on MLX's allocator): for callers that cannot hand
  * over a device workspace or must not allocate between decode steps.

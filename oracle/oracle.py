@@ -23,7 +23,7 @@ __all__ = [
     "lib", "build", "Proc", "Sampler", "expf", "q52", "exp64", "log64", "philox4x32_10",
     "gumbel_from_word", "u53", "row_lse", "tile_stats", "process", "logprobs", "sample",
     "verify", "bf16_to_f32", "philox_gumbel", "philox_uniform", "window_start",
-    "shard_sample",
+    "shard_sample", "draft_ngram",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -548,3 +548,33 @@ def shard_sample(logits_shards: Sequence[np.ndarray], sampler: Sampler, gumbel=N
                               seed, offset, b)
         toks[b] = _sample_one(full[b], lses[b], sampler, nz)[0]
     return toks, np.array(lses, dtype=np.float32)
+
+
+def draft_ngram(tokens, k: int, n_min: int = 3, n_max: int = 8):
+    """Draft continuation of the longest recent n-gram match (reference
+    pagedmoe/lookup_decode.py:184-221): for n from min(n_max, len) down to
+    n_min, look for earlier occurrences of the last n tokens that leave at
+    least one token after them; the latest occurrence with a full k tokens
+    after it wins, else the occurrence with the most tokens after it (the
+    earliest); the first n with any occurrence decides.  Returns (draft,
+    matched_n) with ([], 0) when nothing matches."""
+    toks = [int(t) for t in tokens]
+    L = len(toks)
+    if k <= 0:
+        return [], 0
+    for n in range(min(n_max, L), n_min - 1, -1):
+        tail = toks[L - n:]
+        full, part = None, None
+        for s in range(L - n):  # s + n <= L - 1: something follows
+            if toks[s:s + n] != tail:
+                continue
+            if s + n + k <= L:
+                full = s  # keep the latest
+            elif part is None:
+                part = s  # the earliest partial has the longest continuation
+        if full is not None:
+            return toks[full + n:full + n + k], n
+        if part is not None:
+            return toks[part + n:L], n
+    return [], 0
+

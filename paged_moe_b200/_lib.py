@@ -115,6 +115,7 @@ SIGNATURES = {
     "pm_shard_summary_bytes": (C.c_size_t, [_P, _P]),
     "pm_shard_summarize": (C.c_int, [_P, _P, _P, _P, _P, C.c_size_t, _P]),
     "pm_shard_merge": (C.c_int, [_P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
+    "pm_draft_ngram": (C.c_int, [_P, _P, C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P]),
 }
 
 _lib = None

@@ -589,6 +589,7 @@ __global__ void k_bias_offsets(const int32_t* tok, int n, int n_tiles, int32_t* 
 #include "pm_wide.cuh"
 #include "pm_verify_impl.cuh"
 #include "pm_shard_impl.cuh"
+#include "pm_ngram.cuh"
 
 // ============================================================================
 // host side
@@ -1382,6 +1383,27 @@ int pm_shard_merge(const pm_rows* rows, const pm_shard* shard, const pm_noise* n
 }
 
 }  // extern "C"
+
+extern "C" int pm_draft_ngram(const int32_t* hist, const int32_t* hist_len, int64_t hist_stride,
+                              int64_t requests, int32_t k, int32_t n_min, int32_t n_max, int32_t* drafts,
+                              int32_t* draft_len, int32_t* match_n, void* stream) {
+  if (requests < 0 || k < 0 || n_min < 1 || n_max > pm::kNgramMax || hist_stride < 0) return PM_ERR_ARG;
+  if (requests == 0 || k == 0) {
+    if (requests > 0 && draft_len) {
+      cudaError_t e = cudaMemsetAsync(draft_len, 0, sizeof(int32_t) * requests, reinterpret_cast<cudaStream_t>(stream));
+      if (e == cudaSuccess && match_n)
+        e = cudaMemsetAsync(match_n, 0, sizeof(int32_t) * requests, reinterpret_cast<cudaStream_t>(stream));
+      return e == cudaSuccess ? PM_OK : cuda_fail(e);
+    }
+    return PM_OK;
+  }
+  if (!hist || !drafts || !draft_len) return PM_ERR_ARG;
+  int64_t grid = requests < (int64_t)num_sms() * 8 ? requests : (int64_t)num_sms() * 8;
+  pm::k_draft_ngram<<<(unsigned)grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      hist, hist_len, hist_stride, requests, k, n_min, n_max, drafts, draft_len, match_n);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PM_OK : cuda_fail(e);
+}
 
 // ============================================================================
 // Fixed-scratch variant of pm_sample_rows

@@ -98,3 +98,11 @@ def test_sampling_defaults_match_reference():
         applied = S.fill(h, fcase["body"], fcase["defaults"], argv=fcase["argv"])
         assert applied == fcase["applied"]
         assert vars(h) == fcase["handler"]
+
+
+def test_ngram_draft_matches_reference():
+    """lookup_decode.draft_ngram (reference lookup_decode.py:184-221) on the
+    fixture's 209 contexts."""
+    g = json.load(open(os.path.join(GOLDEN, "draft_ngram.json")))
+    for c in g["cases"]:
+        assert O.draft_ngram(c["tokens"], c["k"], g["ngram_min"], g["ngram_max"])[0] == c["out"], c
