@@ -119,6 +119,10 @@ typedef struct pm_rows {
      * every row's flags, and the largest top_k of any row (0 if none). */
     uint32_t flags_any;
     int32_t top_k_max;
+    /* forced token per row, -1 for none, or NULL: the row's logits become
+     * where(arange == forced, logits, -inf) after the other processors (the
+     * ThinkBudget processor, reference think_budget.py:107-109) */
+    const int32_t *forced;
 } pm_rows;
 
 /* Noise of the draw. */
@@ -232,6 +236,20 @@ PM_API int pm_shard_merge(const pm_rows *rows, const pm_shard *shard, const pm_n
 PM_API int pm_draft_ngram(const int32_t *hist, const int32_t *hist_len, int64_t hist_stride, int64_t requests,
                           int32_t k, int32_t n_min, int32_t n_max, int32_t *drafts, int32_t *draft_len,
                           int32_t *match_n, void *stream);
+
+/* Device ThinkBudget (reference pagedmoe/think_budget.py:75-109): for every
+ * row, the token the close text forces next, or -1.  gen: [rows, gen_stride]
+ * ids generated after the prompt (gen_len per row); piece_len / piece_end:
+ * [table_size] decoded length and sentence-end flag per id; chars: per-row
+ * budget; close: [n_close] ids ending with end_id; start_id < 0 when the
+ * template opens reasoning in the prompt (open_in_prompt) -- else reasoning
+ * counts only after the model's own start_id; slack: tokens to wait for a
+ * sentence end (reference SLACK_TOKENS = 48).  forced: [rows] out, usable as
+ * pm_rows.forced. */
+PM_API int pm_think_budget(const int32_t *gen, const int32_t *gen_len, int64_t gen_stride, int64_t rows,
+                           const int32_t *piece_len, const uint8_t *piece_end, int64_t table_size,
+                           const int32_t *chars, const int32_t *close, int32_t n_close, int32_t end_id,
+                           int32_t start_id, int32_t slack, int32_t *forced, void *stream);
 
 /* pm_sample_rows on scratch owned by the library (no counterpart in the
  * reference, which runs on MLX's allocator): for callers that cannot hand

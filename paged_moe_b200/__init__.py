@@ -15,7 +15,7 @@ from .params import ProcessorSettings, SamplerSettings  # noqa: F401
 
 _lib.load()
 
-from .engine import apply_processors, logprobs, sample_rows  # noqa: E402,F401
+from .engine import apply_processors, argmax_confidence, logprobs, sample_rows  # noqa: E402,F401
 from .sample_utils import make_logits_processors, make_sampler  # noqa: E402,F401
 from .verify import verify  # noqa: E402,F401
 

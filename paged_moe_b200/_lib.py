@@ -64,7 +64,7 @@ class Rows(C.Structure):
         ("feed", C.c_void_p), ("feed_group", C.c_int32),
         ("bias_tokens", C.c_void_p), ("bias_values", C.c_void_p), ("n_bias", C.c_int32),
         ("mask", C.c_void_p), ("mask_stride", C.c_int64),
-        ("flags_any", C.c_uint32), ("top_k_max", C.c_int32),
+        ("flags_any", C.c_uint32), ("top_k_max", C.c_int32), ("forced", C.c_void_p),
     ]
 
 
@@ -115,6 +115,8 @@ SIGNATURES = {
     "pm_shard_summary_bytes": (C.c_size_t, [_P, _P]),
     "pm_shard_summarize": (C.c_int, [_P, _P, _P, _P, _P, C.c_size_t, _P]),
     "pm_shard_merge": (C.c_int, [_P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
+    "pm_think_budget": (C.c_int, [_P, _P, C.c_int64, C.c_int64, _P, _P, C.c_int64, _P, _P, C.c_int32, C.c_int32,
+                                  C.c_int32, C.c_int32, _P, _P]),
     "pm_draft_ngram": (C.c_int, [_P, _P, C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P]),
 }
 

@@ -590,6 +590,7 @@ __global__ void k_bias_offsets(const int32_t* tok, int n, int n_tiles, int32_t* 
 #include "pm_verify_impl.cuh"
 #include "pm_shard_impl.cuh"
 #include "pm_ngram.cuh"
+#include "pm_force.cuh"
 
 // ============================================================================
 // host side
@@ -898,8 +899,19 @@ int launch_rows(const pm_rows* r, int KC, const pm::SampleArgs& a, cudaStream_t 
   } else {
     rc = launch_stream_any(r->dtype, KC, a, has_cand_rows(r), st);
   }
-  if (rc || !(r->flags_any & PM_F_UNBOUNDED)) return rc;
-  return bf ? launch_wide<__nv_bfloat16>(a, st) : launch_wide<float>(a, st);
+  if (rc) return rc;
+  if (r->flags_any & PM_F_UNBOUNDED) {
+    rc = bf ? launch_wide<__nv_bfloat16>(a, st) : launch_wide<float>(a, st);
+    if (rc) return rc;
+  }
+  if (r->forced) {
+    int64_t grid = (a.rows + 255) / 256;
+    if (grid > (int64_t)num_sms() * 4) grid = (int64_t)num_sms() * 4;
+    pm::k_force_rows<<<(unsigned)grid, 256, 0, st>>>(a, r->dtype, r->forced);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
+  return PM_OK;
 }
 
 int check_noise(const pm_rows* rows, const pm_noise* noise) {
@@ -1401,6 +1413,22 @@ extern "C" int pm_draft_ngram(const int32_t* hist, const int32_t* hist_len, int6
   int64_t grid = requests < (int64_t)num_sms() * 8 ? requests : (int64_t)num_sms() * 8;
   pm::k_draft_ngram<<<(unsigned)grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       hist, hist_len, hist_stride, requests, k, n_min, n_max, drafts, draft_len, match_n);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PM_OK : cuda_fail(e);
+}
+
+extern "C" int pm_think_budget(const int32_t* gen, const int32_t* gen_len, int64_t gen_stride, int64_t rows,
+                               const int32_t* piece_len, const uint8_t* piece_end, int64_t table_size,
+                               const int32_t* chars, const int32_t* close, int32_t n_close, int32_t end_id,
+                               int32_t start_id, int32_t slack, int32_t* forced, void* stream) {
+  if (rows < 0 || gen_stride < 0 || table_size <= 0 || n_close <= 0 || slack < 0) return PM_ERR_ARG;
+  if (rows == 0) return PM_OK;
+  if (!gen || !piece_len || !piece_end || !chars || !close || !forced) return PM_ERR_ARG;
+  int64_t grid = (rows + 7) / 8;
+  if (grid > (int64_t)num_sms() * 8) grid = (int64_t)num_sms() * 8;
+  pm::k_think_budget<<<(unsigned)grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      gen, gen_len, gen_stride, rows, piece_len, piece_end, table_size, chars, close, n_close, end_id, start_id,
+      slack, forced);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? PM_OK : cuda_fail(e);
 }

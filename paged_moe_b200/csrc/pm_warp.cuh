@@ -41,30 +41,30 @@ __device__ __forceinline__ void cand_compact(uint64_t* buf, unsigned* hist, Cand
 }
 
 // Offer VW consecutive values per lane (tokens tok0 .. tok0+VW-1; lmax their
-// maximum) to the buffer.  One vote per group in the common case.
+// maximum) to the buffer.  One vote per group in the common case; a group
+// that passes writes its keys by one ballot per value position (no scan).
 template <int VW, int CAP>
 __device__ __forceinline__ bool cand_offer_vec(const float (&x)[VW], float lmax, uint32_t tok0, uint64_t* buf,
                                                unsigned* hist, Cand& c, int K) {
   const int lane = threadIdx.x & 31;
   if (!__any_sync(kFull, lmax > -INFINITY && lmax >= c.tau_x)) return false;
-  unsigned valid = 0;
+  const unsigned below = (1u << lane) - 1u;
+  int base = c.cnt;
 #pragma unroll
-  for (int i = 0; i < VW; ++i)
-    if (x[i] > -INFINITY && x[i] >= c.tau_x && rankkey(x[i], tok0 + i) > c.tau) valid |= 1u << i;
-  const int nv = __popc(valid);
-  const int incl = warp_incl_scan(nv);
-  int pos = c.cnt + incl - nv;
-#pragma unroll
-  for (int i = 0; i < VW; ++i)
-    if ((valid >> i) & 1u) buf[pos++] = rankkey(x[i], tok0 + i);
-  c.cnt += __shfl_sync(kFull, incl, 31);
+  for (int i = 0; i < VW; ++i) {
+    const uint64_t key = rankkey(x[i], tok0 + i);
+    const bool ok = x[i] > -INFINITY && x[i] >= c.tau_x && key > c.tau;
+    const unsigned bal = __ballot_sync(kFull, ok);
+    if (ok) buf[base + __popc(bal & below)] = key;
+    base += __popc(bal);
+  }
+  c.cnt = base;
   __syncwarp();
-  // the first compaction comes early (2K keys) to set a useful threshold
-  if (c.cnt > (c.trimmed ? CAP - 32 * VW : min(CAP - 32 * VW, 2 * K))) {
+  // the first compaction comes early (K + 256 keys) to set a useful threshold
+  if (c.cnt > (c.trimmed ? CAP - 32 * VW : min(CAP - 32 * VW, K + 256))) {
     cand_compact<CAP>(buf, hist, c, K);
     return true;
   }
-  (void)lane;
   return false;
 }
 

@@ -110,7 +110,8 @@ def _params_for(dev: torch.device, sampler, processors, B: int, V: int):
 
 
 def build_rows(logits: torch.Tensor, sampler, processors, history, history_len, mask, keep: _Keep,
-               feed: Optional[torch.Tensor] = None, feed_group: int = 0) -> L.Rows:
+               feed: Optional[torch.Tensor] = None, feed_group: int = 0,
+               forced: Optional[torch.Tensor] = None) -> L.Rows:
     if logits.dim() != 2:
         raise ValueError("logits must be [rows, vocab]")
     if not logits.is_cuda:
@@ -162,6 +163,9 @@ def build_rows(logits: torch.Tensor, sampler, processors, history, history_len, 
             raise ValueError("mask has fewer than ceil(vocab/32) words per row")
         r.mask = m.data_ptr()
         r.mask_stride = m.shape[1]
+    if forced is not None:
+        f = keep(torch.as_tensor(forced, device=dev).to(torch.int32).reshape(B).contiguous())
+        r.forced = f.data_ptr()
     keep(logits)
     return r
 
@@ -189,18 +193,20 @@ def sample_rows(logits: torch.Tensor, sampler: Union[SamplerSettings, Sequence[S
                 history: Optional[torch.Tensor] = None, history_len=None, mask: Optional[torch.Tensor] = None,
                 seed: int = 0, offset: int = 0, row_base: int = 0, gumbel: Optional[torch.Tensor] = None,
                 uniform: Optional[torch.Tensor] = None, return_lse: bool = False,
-                return_logprob: bool = False, survivors: int = 0, return_status: bool = False):
+                return_logprob: bool = False, survivors: int = 0, return_status: bool = False,
+                forced: Optional[torch.Tensor] = None):
     """Processors + log-softmax + sampler for every row, one fused pass.
 
     Returns a dict with "tokens" [B] int32 (and "lse", "logprob",
     "surv_ids"/"surv_probs"/"n_surv" when asked), all on the logits' device,
     enqueued on the current stream.  "status" [B] is non-zero for a row whose
-    settings fell outside the fused path's limits.
+    settings fell outside the fused path's limits.  forced [B] (-1: none)
+    restricts a row to one token (the ThinkBudget hook).
     """
     keep = _Keep()
     lib = L.load()
     dev = logits.device
-    r = build_rows(logits, sampler, processors, history, history_len, mask, keep)
+    r = build_rows(logits, sampler, processors, history, history_len, mask, keep, forced=forced)
     B, V = r.rows, r.vocab
     nz = _noise(B, V, seed, offset, row_base, gumbel, uniform, keep, dev)
     out = L.SampleOut()
@@ -273,3 +279,13 @@ def logprobs(logits: torch.Tensor, processors=None, history=None, history_len=No
                          stream.cuda_stream)
     L.check(rc, "pm_logprobs")
     return out, lse
+
+
+def argmax_confidence(logits: torch.Tensor, processors=None, history=None, mask=None):
+    """Greedy token and its softmax probability per row: the reduction of
+    each MTP draft-chain step (reference pagedmoe/mtp.py:731-746, argmax and
+    max(softmax)), in one pass: tokens [B] int32, confidence [B] fp32."""
+    res = sample_rows(logits, SamplerSettings(temp=0.0), processors, history=history, mask=mask,
+                      return_logprob=True)
+    return res["tokens"], torch.exp(res["logprob"])
+
