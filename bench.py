@@ -46,7 +46,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", default="c3", choices=["c3", "c5"],
+    ap.add_argument("--workload", default="c3", choices=["c3", "c5", "c1", "c2", "c2b", "c4a", "c4b"],
                     help="c3 (default): the headline metric's config; c5: vocabulary-sharded sampling over the ranks")
     return ap.parse_args()
 
@@ -423,12 +423,114 @@ def run_c5(args):
     print(json.dumps(line), flush=True)
 
 
+def run_config(args):
+    """The other BASELINE configs on one GPU (reported beside the headline):
+    c1 (B=1 latency), c2 / c2b (bf16, 4,096-id Zipf histories, greedy / min_p),
+    c4a / c4b (verify of 32 requests x 5 rows, residual / match)."""
+    import numpy as np
+    import torch
+
+    import paged_moe_b200 as pm
+    from paged_moe_b200 import workloads as W
+    from paged_moe_b200.params import SamplerSettings
+    dev = torch.device("cuda", 0)
+    wl = args.workload
+    if wl == "c1":
+        ds = [W.c1(seed=k) for k in range(2)]
+        xs = [torch.from_numpy(d["logits"]).to(dev) for d in ds]
+        hs = [torch.from_numpy(d["hist"]).to(dev) for d in ds]
+        s, p = ds[0]["sampler"], ds[0]["proc"]
+        rows, nbytes = 1, 151936 * 4 + 256 * 4
+
+        def step(i):
+            return pm.sample_rows(xs[i & 1], s, p, history=hs[i & 1], seed=5, offset=i)
+        desc = "C1: B=1, V=151,936 fp32, temp 0.7, top_k 20, top_p 0.8, repetition 1.05 over 256 ids"
+    elif wl in ("c2", "c2b"):
+        ds = [W.c2(seed=k, second=(wl == "c2b")) for k in range(2)]
+        xs = [torch.from_numpy(d["logits_bf16"].view(np.int16)).to(dev).view(torch.bfloat16) for d in ds]
+        hs = [torch.from_numpy(d["hist"]).to(dev) for d in ds]
+        s, p = ds[0]["sampler"], ds[0]["proc"]
+        rows, nbytes = 64, 64 * (151936 * 2 + 4096 * 4)
+
+        def step(i):
+            return pm.sample_rows(xs[i & 1], s, p, history=hs[i & 1], seed=5, offset=i)
+        desc = ("C2: B=64, V=151,936 bf16, 4,096-id Zipf histories, presence 0.5 + frequency 0.3, "
+                + ("min_p 0.05 at temp 1" if wl == "c2b" else "argmax"))
+    else:
+        ds = [W.c4(seed=k) for k in range(2)]
+        tg = [torch.from_numpy(d["target"]).to(dev) for d in ds]
+        dl = [torch.from_numpy(d["draft_logits"]).to(dev) for d in ds]
+        dr = [torch.from_numpy(d["drafts"]).to(dev) for d in ds]
+        yy = [torch.from_numpy(d["y"]).to(dev) for d in ds]
+        ua = [torch.from_numpy(d["u_accept"]).to(dev) for d in ds]
+        ur = [torch.from_numpy(d["u_residual"]).to(dev) for d in ds]
+        resid = wl == "c4a"
+        s = SamplerSettings(temp=1.0) if resid else SamplerSettings(temp=0.0)
+        rows = 32 * 5
+        nbytes = 32 * (5 + (4 if resid else 0)) * 151552 * 4
+
+        def step(i):
+            k = i & 1
+            if resid:
+                return pm.verify(tg[k], dr[k], yy[k], s, mode="residual", draft_logits=dl[k], u_accept=ua[k],
+                                 u_residual=ur[k], seed=5, offset=i)
+            return pm.verify(tg[k], dr[k], yy[k], s, mode="match", seed=5, offset=i)
+        desc = ("C4: verify of 32 requests x (k=4 drafts + 1) rows, V=151,552 fp32, "
+                + ("residual rejection sampling at temp 1 (p and q rows read)" if resid else
+                   "greedy exact-match acceptance"))
+    stream = torch.cuda.current_stream(dev)
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with Clocks(0) as clk:
+        ev[0].record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize(dev)
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    # the same steps replayed from a CUDA graph (no host work between them)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(8):
+            step(1000 + i)
+    g.replay()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(4):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    graph_us = e0.elapsed_time(e1) * 1000 / 32
+    del g
+    peak, peak_kind = peaks()
+    ms = statistics.mean(per)
+    line = {
+        "metric": f"sampled rows/s ({wl.upper()}); p50 us/step", "value": rows / (ms / 1000.0), "unit": "rows/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": desc},
+        "p50_us_per_step": 1000 * statistics.median(per),
+        "graph_us_per_step": graph_us,
+        "roofline": {"bound": "hbm", "achieved": nbytes / (graph_us * 1e-6) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": nbytes / (graph_us * 1e-6) / 1e9 / peak, "traffic": None,
+                     "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs", "algorithmic_bytes_per_launch": nbytes,
+                     "timing": "graph replay"},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "c5":
         run_c5(args)
+    elif args.workload != "c3":
+        run_config(args)
     else:
         run_ours(args)
 

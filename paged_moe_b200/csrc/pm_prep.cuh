@@ -42,7 +42,7 @@ __device__ __forceinline__ int window_start(int H, int ctx) {
   return (-ctx) < H ? -ctx : H;
 }
 
-// one CTA of 1024 threads per row; dynamic shared memory: cap u64 keys + 32 ints
+// one CTA of 1024 threads per row; dynamic shared memory: cap u64 keys, 64 ints, cap ints
 __global__ void __launch_bounds__(1024) k_prep_overrides(PrepArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);
@@ -93,35 +93,80 @@ __global__ void __launch_bounds__(1024) k_prep_overrides(PrepArgs a) {
       __syncthreads();
     }
   }
-  // each thread owns a contiguous block of E entries
+  // Runs of equal ids are contiguous and ascending by position.  A run's
+  // last element carries its latest position (the repetition / presence
+  // windows) and, through two block scans, the run's first index and the
+  // number of its positions inside the frequency window.  Each thread owns a
+  // contiguous block of E entries.
   const int E = a.cap / nth > 0 ? a.cap / nth : 1;
   const int lo = tid * E;
+  int* fpre = reinterpret_cast<int*>(wsum + 64);  // inclusive count of in-window positions, per entry
+  int fsum = 0, smax = 0;
+  for (int e = 0; e < E; ++e) {
+    const int i = lo + e;
+    if (i >= a.cap) break;
+    const uint64_t k = keys[i];
+    const bool valid = k != ~0ull;
+    if (valid && (i == 0 || (uint32_t)(keys[i - 1] >> 32) != (uint32_t)(k >> 32))) smax = i;
+    fsum += (valid && freq && (int)(uint32_t)k >= s_freq) ? 1 : 0;
+  }
+  // block scans: exclusive sum of in-window counts, exclusive max of run starts
+  {
+    const int lane = tid & 31, wid = tid >> 5;
+    int is = fsum, im = smax;  // warp-inclusive
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int ts = __shfl_up_sync(kFull, is, o), tm = __shfl_up_sync(kFull, im, o);
+      if (lane >= o) { is += ts; im = max(im, tm); }
+    }
+    if (lane == 31) { wsum[wid] = is; wsum[32 + wid] = im; }
+    __syncthreads();
+    if (wid == 0) {
+      const int nw2 = nth >> 5;
+      int xs = lane < nw2 ? wsum[lane] : 0, xm = lane < nw2 ? wsum[32 + lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int ts = __shfl_up_sync(kFull, xs, o), tm = __shfl_up_sync(kFull, xm, o);
+        if (lane >= o) { xs += ts; xm = max(xm, tm); }
+      }
+      if (lane < nw2) { wsum[lane] = xs; wsum[32 + lane] = xm; }
+    }
+    __syncthreads();
+    const int prev_m = __shfl_up_sync(kFull, im, 1);
+    fsum = (is - fsum) + (wid > 0 ? wsum[wid - 1] : 0);
+    smax = max(lane > 0 ? prev_m : 0, wid > 0 ? wsum[32 + wid - 1] : 0);
+  }
+  __syncthreads();  // wsum is reused for the emit scan below
+  int run_start[8];
   int emit_local = 0;
   uint32_t info_loc[8];
   int tok_loc[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) { info_loc[e] = 0; tok_loc[e] = -1; }
+  for (int e = 0; e < 8; ++e) { info_loc[e] = 0; tok_loc[e] = -1; run_start[e] = 0; }
+  for (int e = 0; e < E && e < 8; ++e) {
+    const int i = lo + e;
+    if (i >= a.cap) break;
+    const uint64_t k = keys[i];
+    const bool valid = k != ~0ull;
+    if (valid && (i == 0 || (uint32_t)(keys[i - 1] >> 32) != (uint32_t)(k >> 32))) smax = i;
+    run_start[e] = smax;
+    fsum += (valid && freq && (int)(uint32_t)k >= s_freq) ? 1 : 0;
+    fpre[i] = fsum;
+  }
+  __syncthreads();
   for (int e = 0; e < E && e < 8; ++e) {
     const int i = lo + e;
     if (i >= a.cap) break;
     const uint64_t k = keys[i];
     if (k == ~0ull) continue;
     const uint32_t tok = (uint32_t)(k >> 32);
-    if (i > 0 && (uint32_t)(keys[i - 1] >> 32) == tok) continue;  // not a run start
-    int end = i + 1;
-    while (end < a.cap && (uint32_t)(keys[end] >> 32) == tok) ++end;
-    const int last_pos = (int)(uint32_t)keys[end - 1];
+    if (i + 1 < a.cap && keys[i + 1] != ~0ull && (uint32_t)(keys[i + 1] >> 32) == tok) continue;  // not a run end
+    const int last_pos = (int)(uint32_t)k;
+    const int st = run_start[e];
     uint32_t info = 0;
     if (rep && last_pos >= s_rep) info |= 1u;
     if (pres && last_pos >= s_pres) info |= 2u;
-    if (freq) {
-      int lo2 = i, hi2 = end;  // first position >= s_freq within the run
-      while (lo2 < hi2) {
-        const int mid = (lo2 + hi2) >> 1;
-        if ((int)(uint32_t)keys[mid] >= s_freq) hi2 = mid; else lo2 = mid + 1;
-      }
-      info |= (uint32_t)(end - lo2) << 8;
-    }
+    if (freq) info |= (uint32_t)(fpre[i] - (st > 0 ? fpre[st - 1] : 0)) << 8;
     if (info) { info_loc[e] = info; tok_loc[e] = (int)tok; ++emit_local; }
   }
   // block exclusive scan of emit counts

@@ -398,20 +398,133 @@ __device__ __forceinline__ void write_row(const SampleArgs& a, int64_t row, int 
   if (a.n_surv && (mode != kCand || !a.surv_ids)) a.n_surv[row] = mode == kCand ? ns : 0;
 }
 
-// Merge of every row's parts: one warp per row.  Launched after the
-// streaming kernel on the same stream (programmatic dependent launch: it may
-// start while the streaming kernel drains, and waits for its results).
+// Merge of every row's parts: one CTA (8 warps) per row.  Launched after
+// the streaming kernel on the same stream (programmatic dependent launch: it
+// may start while the streaming kernel drains, and waits for its results).
+// For a filtered row each warp folds every eighth part's candidates into
+// its own top-K buffer, the CTA radix-selects the row's top-K from the eight
+// lists, warp 0 finishes the log-sum-exp while the other warps compute the
+// candidates' Gumbel scores, and warp 0 filters and draws.  Greedy and
+// whole-vocabulary rows are merged by warp 0 alone.
+template <int KC>
+struct MergeCta {
+  static constexpr int CAP = StreamMem<KC>::CAP;
+  uint64_t cand[8][CAP];
+  unsigned hist[8][256];
+  uint64_t u[8 * KC];
+  uint64_t carry[KC];
+  float score[KC];
+  unsigned mhist[256];
+  int scal[8];
+  int wcnt[8];
+  int wtrim[8];
+  float lse;
+};
+
 template <typename T, int KC>
-__global__ void __launch_bounds__(256) k_row_merge(const __grid_constant__ SampleArgs a) {
+__global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ SampleArgs a) {
+  using M = MergeCta<KC>;
+  constexpr int CAP = M::CAP;
+  extern __shared__ __align__(128) unsigned char smem_merge[];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  M* mc = reinterpret_cast<M*>(smem_merge);
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int64_t total = a.rows * a.n_tiles;
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int n_parts = (int)(owner_warp((row + 1) * a.n_tiles - 1, total, a.n_warps) -
+                              owner_warp(row * a.n_tiles, total, a.n_warps) + 1);
+    const pm_row_params p = row_params(a, row);
+    const int mode = row_mode(p);
+    if (mode != kCand) {
+      if (wid == 0) {
+        float x_tok, lse;
+        int ns;
+        const int tok = warp_row_merge<T, KC, CAP>(a, row, n_parts, mc->cand[0], mc->hist[0], &x_tok, &lse, &ns);
+        if (lane == 0) write_row(a, row, mode, tok, x_tok, lse, ns);
+      }
+      __syncthreads();
+      continue;
+    }
+    const int K = (p.top_k > 0 && p.top_k < KC) ? p.top_k : KC;
+    // 1. each warp: parts wid, wid + 8, ... into its own top-K
+    {
+      Cand cd;
+      cand_reset(cd);
+      bool trimmed = false;
+      for (int part = wid; part < n_parts; part += 8) {
+        const int raw = ld_cg(&a.cand_n[row * a.max_parts + part]);
+        trimmed |= ((raw >> 30) & 1) != 0;
+        const int n = raw & 0x3fffffff;
+        const uint64_t* src = a.cand + (row * a.max_parts + part) * (int64_t)KC;
+        for (int i0 = 0; i0 < n; i0 += 32)
+          cand_offer_key<CAP>(i0 + lane < n ? ld_cg(&src[i0 + lane]) : 0ull, mc->cand[wid], mc->hist[wid], cd, K);
+      }
+      if (cd.cnt > K) cand_compact<CAP>(mc->cand[wid], mc->hist[wid], cd, K);
+      for (int i = lane; i < cd.cnt; i += 32) mc->u[wid * KC + i] = mc->cand[wid][i];
+      if (lane == 0) { mc->wcnt[wid] = cd.cnt; mc->wtrim[wid] = trimmed || cd.trimmed; }
+    }
+    __syncthreads();
+    // 2. the eight lists end to end, then the row's top-K sorted into the carry
+    int tot = 0, start[8];
+    bool dropped = false;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      start[w] = tot;
+      tot += mc->wcnt[w];
+      dropped |= mc->wtrim[w] != 0;
+    }
+    uint64_t mine[8];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) mine[w] = tid < mc->wcnt[w] ? mc->u[w * KC + tid] : 0ull;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < 8; ++w)
+      if (tid < mc->wcnt[w]) mc->u[start[w] + tid] = mine[w];
+    __syncthreads();
+    dropped |= tot > K;
+    const int ncarry = block_topk_sorted(mc->u, tot, K, mc->carry, KC, mc->mhist, mc->scal);
+    __syncthreads();
+    // 3. log-sum-exp (warp 0) beside the Gumbel scores (the other warps)
+    const bool needx = needs_xstats(a, p, mode);
+    if (wid == 0 && needx) {
+      float mx;
+      const float c = warp_combine(a.statx + row * a.n_tiles, a.n_tiles, &mx);
+      if (lane == 0) mc->lse = c;
+    }
+    for (int r = tid - 32; r >= 0 && r < ncarry; r += 256 - 32)
+      mc->score[r] = fadd(fmul(key_value(mc->carry[r]), p.inv_temperature), row_gumbel(a, row, key_index(mc->carry[r])));
+    __syncthreads();
+    // 4. filters and draw
+    if (wid == 0) {
+      const float c = needx ? mc->lse : __int_as_float(0x7fc00000);
+      int ns = 0;
+      const int tok = warp_filter_draw(a, p, row, mc->carry, ncarry, !dropped, c, &ns, mc->score);
+      float x_tok = -INFINITY;
+      if (tok >= 0) {
+        float fx = -INFINITY;
+        for (int r = lane; r < ncarry; r += 32)
+          if ((int)key_index(mc->carry[r]) == tok) fx = key_value(mc->carry[r]);
+        x_tok = warp_max(fx);
+        if (a.surv_ids && lane == 0) write_survivors(a, p, row, mc->carry, ns);
+      }
+      if (lane == 0) write_row(a, row, mode, tok, x_tok, c, ns);
+    }
+    __syncthreads();
+  }
+}
+
+// Merge with one warp per row: for many rows with few parts each.
+template <typename T, int KC>
+__global__ void __launch_bounds__(256) k_row_merge_warp(const __grid_constant__ SampleArgs a) {
   constexpr int CAP = StreamMem<KC>::CAP;
   struct MergeMem {
     uint64_t cand[CAP];
     unsigned hist[256];
   };
-  extern __shared__ __align__(128) unsigned char smem_merge[];
+  extern __shared__ __align__(128) unsigned char smem_mwarp[];
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  MergeMem* mm = reinterpret_cast<MergeMem*>(smem_merge) + wid;
+  MergeMem* mm = reinterpret_cast<MergeMem*>(smem_mwarp) + wid;
   const int64_t total = a.rows * a.n_tiles;
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + wid; row < a.rows;
        row += (int64_t)gridDim.x * (blockDim.x >> 5)) {
@@ -771,10 +884,10 @@ int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::Sample
     pa.ovr_info = reinterpret_cast<uint32_t*>(ws + L.ovr_info);
     pa.ovr_off = reinterpret_cast<int32_t*>(ws + L.ovr_off);
     pa.status = a.status;
-    const size_t smem = sizeof(uint64_t) * L.ovr_cap + 64 * sizeof(int);
+    const size_t smem = sizeof(uint64_t) * L.ovr_cap + 64 * sizeof(int) + sizeof(int) * L.ovr_cap;
     static std::once_flag once;
     std::call_once(once, [] {
-      cudaFuncSetAttribute(pm::k_prep_overrides, cudaFuncAttributeMaxDynamicSharedMemorySize, 8192 * 8 + 256);
+      cudaFuncSetAttribute(pm::k_prep_overrides, cudaFuncAttributeMaxDynamicSharedMemorySize, 8192 * 12 + 256);
     });
     pm::k_prep_overrides<<<(unsigned)r->rows, 1024, smem, st>>>(pa);
     e = cudaGetLastError();
@@ -815,19 +928,24 @@ int launch_stream(const pm::SampleArgs& a, bool cand_rows, cudaStream_t st, bool
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   if (!merge) return PM_OK;
-  // the row merges: one warp per row, chained by programmatic dependent launch
-  constexpr int kMergeWarps = 8;
-  const size_t msmem = (sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * kMergeWarps;
+  // the row merges, chained by programmatic dependent launch: one CTA per
+  // row when rows are few (every row then has many parts), one warp per row
+  // otherwise
+  const bool per_cta = a.rows <= (int64_t)num_sms() * 2;
+  const size_t msmem = per_cta ? sizeof(pm::MergeCta<KC>) : (sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * 8;
   static std::once_flag once;
-  std::call_once(once, [msmem] {
-    cudaFuncSetAttribute(pm::k_row_merge<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem);
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(pm::k_row_merge_cta<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sizeof(pm::MergeCta<KC>));
+    cudaFuncSetAttribute(pm::k_row_merge_warp<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)((sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * 8));
   });
-  int64_t mgrid = (a.rows + kMergeWarps - 1) / kMergeWarps;
-  const int64_t mcap = (int64_t)num_sms() * 8;
+  int64_t mgrid = per_cta ? a.rows : (a.rows + 7) / 8;
+  const int64_t mcap = (int64_t)num_sms() * (per_cta ? 3 : 8);
   if (mgrid > mcap) mgrid = mcap;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)mgrid);
-  cfg.blockDim = dim3(32 * kMergeWarps);
+  cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = msmem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -835,10 +953,12 @@ int launch_stream(const pm::SampleArgs& a, bool cand_rows, cudaStream_t st, bool
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, pm::k_row_merge<T, KC>, a);
+  e = per_cta ? cudaLaunchKernelEx(&cfg, pm::k_row_merge_cta<T, KC>, a)
+              : cudaLaunchKernelEx(&cfg, pm::k_row_merge_warp<T, KC>, a);
   if (e != cudaSuccess) {
     cudaGetLastError();  // no programmatic launch here: plain stream order
-    pm::k_row_merge<T, KC><<<(unsigned)mgrid, 32 * kMergeWarps, msmem, st>>>(a);
+    if (per_cta) pm::k_row_merge_cta<T, KC><<<(unsigned)mgrid, 256, msmem, st>>>(a);
+    else pm::k_row_merge_warp<T, KC><<<(unsigned)mgrid, 256, msmem, st>>>(a);
     e = cudaGetLastError();
   }
   return e == cudaSuccess ? PM_OK : cuda_fail(e);
@@ -941,7 +1061,7 @@ struct VLayout {
   Layout L;
   int k = 0, scap = 0;
   int64_t B = 0, D = 0;
-  size_t rtok = 0, sids = 0, sprobs = 0, ns = 0, pending = 0, dstat = 0, dlse = 0, total = 0;
+  size_t rtok = 0, sids = 0, sprobs = 0, ns = 0, pending = 0, dstat = 0, dlse = 0, ylse = 0, rsum = 0, total = 0;
 };
 
 int plan_verify(const pm_rows* r, const pm_verify_args* v, VLayout* V) {
@@ -966,6 +1086,8 @@ int plan_verify(const pm_rows* r, const pm_verify_args* v, VLayout* V) {
   V->pending = take(sizeof(int32_t) * V->B);
   V->dstat = take(sizeof(pm::TileStat) * V->D * V->L.n_tiles);
   V->dlse = take(sizeof(float) * V->D);
+  V->ylse = take(sizeof(float) * V->B);
+  V->rsum = take(res ? sizeof(uint64_t) * V->B * V->L.n_tiles : 0);
   V->total = align_up(o, 256);
   return PM_OK;
 }
@@ -1176,15 +1298,36 @@ int pm_verify(const pm_rows* rows, const pm_noise* noise, const pm_verify_args* 
   vk.ns = a.n_surv;
   vk.scap = V.scap;
   vk.pending = reinterpret_cast<int32_t*>(ws + V.pending);
+  vk.ylse = reinterpret_cast<float*>(ws + V.ylse);
+  vk.rsum = reinterpret_cast<uint64_t*>(ws + V.rsum);
   rc = V.L.KC == 64 ? launch_accept<64>(a, rows->dtype, vk, V.B, st) : launch_accept<256>(a, rows->dtype, vk, V.B, st);
   if (rc) return rc;
   if (res && V.k > 0 && (rows->flags_any & PM_F_FULL)) {
-    int64_t grid = V.B < (int64_t)num_sms() * 4 ? V.B : (int64_t)num_sms() * 4;
-    if (rows->dtype == PM_DTYPE_BF16)
-      pm::k_verify_residual<__nv_bfloat16><<<(unsigned)grid, 256, 0, st>>>(a, vk);
-    else
-      pm::k_verify_residual<float><<<(unsigned)grid, 256, 0, st>>>(a, vk);
+    // the draft rows as plain rows for the tile loads (no processors)
+    pm::SampleArgs da = a;
+    da.logits = v->draft_logits;
+    da.rows = V.D;
+    da.row_stride = v->draft_row_stride;
+    const size_t desz = v->draft_dtype == PM_DTYPE_F32 ? 4 : 2;
+    da.vec_ok = ((uintptr_t)v->draft_logits % 16 == 0) && ((v->draft_row_stride * desz) % 16 == 0);
+    da.mask = nullptr;
+    da.mask_ok = false;
+    da.ovr_off = nullptr;
+    da.bias_off = nullptr;
+    int64_t g1 = (V.B * V.L.n_tiles + 7) / 8;
+    if (g1 > (int64_t)num_sms() * 16) g1 = (int64_t)num_sms() * 16;
+    const bool tb = rows->dtype == PM_DTYPE_BF16, db = v->draft_dtype == PM_DTYPE_BF16;
+    if (tb && db) pm::k_residual_tiles<__nv_bfloat16, __nv_bfloat16><<<(unsigned)g1, 256, 0, st>>>(a, da, vk);
+    else if (tb) pm::k_residual_tiles<__nv_bfloat16, float><<<(unsigned)g1, 256, 0, st>>>(a, da, vk);
+    else if (db) pm::k_residual_tiles<float, __nv_bfloat16><<<(unsigned)g1, 256, 0, st>>>(a, da, vk);
+    else pm::k_residual_tiles<float, float><<<(unsigned)g1, 256, 0, st>>>(a, da, vk);
     cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    int64_t g2 = (V.B + 7) / 8;
+    if (g2 > (int64_t)num_sms() * 8) g2 = (int64_t)num_sms() * 8;
+    if (tb) pm::k_residual_draw<__nv_bfloat16><<<(unsigned)g2, 256, 0, st>>>(a, vk);
+    else pm::k_residual_draw<float><<<(unsigned)g2, 256, 0, st>>>(a, vk);
+    e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
   }
   return PM_OK;

@@ -38,6 +38,8 @@ struct VerifyK {
   const int32_t* ns;       // [B*(k+1)]
   int32_t scap;
   int32_t* pending;        // [B] row awaiting a whole-vocabulary residual draw, -1 if none
+  float* ylse;             // [B] that row's log-sum-exp of y = x / temp
+  uint64_t* rsum;          // [B, n_tiles] residual mass of each tile of that row
 };
 
 __device__ __forceinline__ float draft_value(const VerifyK& v, int64_t drow, int64_t tok) {
@@ -151,6 +153,7 @@ __global__ void __launch_bounds__(256) k_verify_accept(const __grid_constant__ S
       const float cd = ld_cg(&v.dlse[drow]);
       const float q_d = draft_prob(v, drow, d, cd);
       float p_d;
+      float cy = 0.0f;
       if (mode == kGreedy) {
         p_d = ld_cg(&v.rtok[row]) == d ? 1.0f : 0.0f;
       } else if (mode == kCand) {
@@ -165,7 +168,7 @@ __global__ void __launch_bounds__(256) k_verify_accept(const __grid_constant__ S
         p_d = warp_max(f);
       } else {
         float m;
-        const float cy = warp_combine(a.staty + row * a.n_tiles, a.n_tiles, &m);
+        cy = warp_combine(a.staty + row * a.n_tiles, a.n_tiles, &m);
         const float x = processed_value(a, dtype, p, row, d);
         const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
         p_d = det_expf(fsub(y, cy));
@@ -178,7 +181,8 @@ __global__ void __launch_bounds__(256) k_verify_accept(const __grid_constant__ S
         final_tok = survivor_residual<KC>(a, v, b, row, drow, cd, am->key, am->q);
         if (final_tok < 0) final_tok = ld_cg(&v.rtok[row]);
       } else {
-        pend = true;  // whole vocabulary: k_verify_residual draws it
+        pend = true;  // whole vocabulary: k_residual_tiles and k_residual_draw draw it
+        if (lane == 0) v.ylse[b] = cy;
       }
       break;
     }
@@ -196,77 +200,99 @@ __global__ void __launch_bounds__(256) k_verify_accept(const __grid_constant__ S
   }
 }
 
-// Whole-vocabulary residual draw: one CTA per request with a pending row.
-// Tile sums of floor(max(fl32(p - q), 0) 2^52), p = expf(fl32(y - c_y)),
-// q = expf(fl32(d - c_d)); the token is the first (ascending) whose inclusive
-// prefix exceeds floor(u R).  No positive residual: the row's own draw.
-template <typename T>
-__global__ void __launch_bounds__(256) k_verify_residual(const __grid_constant__ SampleArgs a,
-                                                         const __grid_constant__ VerifyK v) {
+// Whole-vocabulary residual draw, tile-parallel.  k_residual_tiles: one
+// warp per (request, tile) of every request with a pending row: the tile's
+// sum of floor(max(fl32(p - q), 0) 2^52), p = expf(fl32(y - c_y)),
+// q = expf(fl32(d - c_d)).  k_residual_draw: one warp per pending request:
+// the tile whose inclusive prefix first exceeds floor(u R), then the token
+// inside it the same way (no positive residual: the row's own draw).
+template <typename T, typename TD>
+__global__ void __launch_bounds__(256) k_residual_tiles(const __grid_constant__ SampleArgs a,
+                                                        const __grid_constant__ SampleArgs da,
+                                                        const __grid_constant__ VerifyK v) {
   constexpr int VW = Lay<T>::VW;
-  __shared__ uint64_t tsum[32 * kMaxPer];
-  __shared__ float s_cy;
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  constexpr bool same = Lay<T>::VW == Lay<TD>::VW;
+  const int lane = threadIdx.x & 31;
   const int K1 = v.k + 1;
   const int64_t B = a.rows / K1;
-  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+  const int nt = a.n_tiles;
+  const int64_t total = B * nt;
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total;
+       w += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    const int64_t b = w / nt;
+    const int t = (int)(w - b * nt);
     const int j = ld_cg(&v.pending[b]);
-    if (j < 0) continue;  // uniform across the CTA
+    if (j < 0) continue;  // warp-uniform
     const int64_t row = b * K1 + j;
     const int64_t drow = b * v.k + j;
     const pm_row_params p = row_params(a, row);
-    if (wid == 0) {
-      float m;
-      const float cy = warp_combine(a.staty + row * a.n_tiles, a.n_tiles, &m);
-      if (lane == 0) s_cy = cy;
-    }
-    __syncthreads();
-    const float cy = s_cy;
+    const float cy = ld_cg(&v.ylse[b]);
     const float cd = ld_cg(&v.dlse[drow]);
-    for (int t = wid; t < a.n_tiles; t += nw) {
-      TileIn ti;
-      load_tile<T>(a, row, t, ti);
-      process_tile_regs<VW>(a, p, row, t, ti);
-      const int64_t start = (int64_t)t * kTile;
-      const int n_valid = tile_valid(a, t);
-      uint64_t s = 0;
+    TileIn ti;
+    load_tile<T>(a, row, t, ti);
+    process_tile_regs<VW>(a, p, row, t, ti);
+    TileIn td;
+    if constexpr (same) load_tile<TD>(da, drow, t, td);
+    const int64_t start = (int64_t)t * kTile;
+    const int n_valid = tile_valid(a, t);
+    uint64_t s = 0;
 #pragma unroll
-      for (int sl = 0; sl < 32; ++sl) {
-        const int e = slot_elem<VW>(sl, lane);
-        if (e < n_valid) {
-          const float x = ti.v[sl];
-          const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
-          s += residual_q52(det_expf(fsub(y, cy)), draft_prob(v, drow, start + e, cd));
-        }
+    for (int sl = 0; sl < 32; ++sl) {
+      const int e = slot_elem<VW>(sl, lane);
+      if (e < n_valid) {
+        const float x = ti.v[sl];
+        const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
+        float dv;
+        if constexpr (same) dv = td.v[sl];
+        else dv = draft_value(v, drow, start + e);
+        s += residual_q52(det_expf(fsub(y, cy)), det_expf(fsub(dv, cd)));
       }
-      s = warp_sum_u64(s);
-      if (lane == 0) tsum[t] = s;
     }
-    __syncthreads();
-    if (wid == 0) {
-      uint64_t R = 0;
-      for (int t = lane; t < a.n_tiles; t += 32) R += tsum[t];
-      R = warp_sum_u64(R);
+    s = warp_sum_u64(s);
+    if (lane == 0) v.rsum[w] = s;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_residual_draw(const __grid_constant__ SampleArgs a,
+                                                       const __grid_constant__ VerifyK v) {
+  constexpr int VW = Lay<T>::VW;
+  const int lane = threadIdx.x & 31;
+  const int K1 = v.k + 1;
+  const int64_t B = a.rows / K1;
+  const int nt = a.n_tiles;
+  for (int64_t b = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < B;
+       b += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    const int j = ld_cg(&v.pending[b]);
+    if (j < 0) continue;
+    const int64_t row = b * K1 + j;
+    const int64_t drow = b * v.k + j;
+    const pm_row_params p = row_params(a, row);
+    const float cy = ld_cg(&v.ylse[b]);
+    const float cd = ld_cg(&v.dlse[drow]);
+    const uint64_t* rs = v.rsum + b * nt;
+    uint64_t R = 0;
+    for (int t = lane; t < nt; t += 32) R += ld_cg(&rs[t]);
+    R = warp_sum_u64(R);
+    int tok = ld_cg(&v.rtok[row]);
+    if (R > 0) {
+      const uint64_t tgt = scale_u53(residual_u53(a, v, b, row), R);
       int tt = -1;
       uint64_t t2 = 0;
-      if (R > 0) {
-        const uint64_t tgt = scale_u53(residual_u53(a, v, b, row), R);
-        uint64_t carry = 0;
-        for (int t0 = 0; t0 < a.n_tiles; t0 += 32) {
-          const int t = t0 + lane;
-          const uint64_t w = t < a.n_tiles ? tsum[t] : 0ull;
-          const uint64_t incl = carry + warp_incl_scan_u64(w);
-          const unsigned hit = __ballot_sync(kFull, t < a.n_tiles && incl > tgt);
-          if (hit) {
-            const int src = __ffs(hit) - 1;
-            tt = t0 + src;
-            t2 = tgt - (__shfl_sync(kFull, incl, src) - __shfl_sync(kFull, w, src));
-            break;
-          }
-          carry = __shfl_sync(kFull, incl, 31);
+      uint64_t carry = 0;
+      for (int t0 = 0; t0 < nt; t0 += 32) {
+        const int t = t0 + lane;
+        const uint64_t wv = t < nt ? ld_cg(&rs[t]) : 0ull;
+        const uint64_t incl = carry + warp_incl_scan_u64(wv);
+        const unsigned hit = __ballot_sync(kFull, t < nt && incl > tgt);
+        if (hit) {
+          const int src = __ffs(hit) - 1;
+          tt = t0 + src;
+          t2 = tgt - (__shfl_sync(kFull, incl, src) - __shfl_sync(kFull, wv, src));
+          break;
         }
+        carry = __shfl_sync(kFull, incl, 31);
       }
-      int tok = ld_cg(&v.rtok[row]);
       if (tt >= 0) {
         TileIn ti;
         load_tile<T>(a, row, tt, ti);
@@ -309,9 +335,9 @@ __global__ void __launch_bounds__(256) k_verify_residual(const __grid_constant__
           acc = __shfl_sync(kFull, incl, 31);
         }
       }
-      if (lane == 0) v.tokens[b * K1 + j] = tok;
     }
-    __syncthreads();
+    if (lane == 0) v.tokens[b * K1 + j] = tok;
+    __syncwarp();
   }
 }
 
