@@ -108,12 +108,9 @@ __device__ float processed_value(const SampleArgs& a, int dtype, const pm_row_pa
   if (a.ovr_off) {
     const int32_t* off = a.ovr_off + row * (int64_t)(a.n_tiles + 1) + tile;
     const int32_t* otok = a.ovr_tok + row * (int64_t)a.ovr_cap;
-    int lo = off[0], hi = off[1];
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (otok[mid] < tok) lo = mid + 1; else hi = mid;
-    }
-    if (lo < off[1] && otok[lo] == tok) {
+    int lo = off[0];
+    while (lo < off[1] && otok[lo] != tok) ++lo;  // a tile's entries are in no particular order
+    if (lo < off[1]) {
       const uint32_t info = a.ovr_info[row * (int64_t)a.ovr_cap + lo];
       if (info & 1u) x = x < 0.0f ? fmul(x, p.repetition_penalty) : __fdiv_rn(x, p.repetition_penalty);
       if (info & 2u) x = fsub(x, p.presence_penalty);

@@ -1,12 +1,12 @@
-// pm_prep.cuh -- the penalty scatter's host-independent half: per-row sorted
+// pm_prep.cuh -- the penalty scatter's host-independent half: per-row
 // override lists built from the token histories.
 //
-// For every row, the ids inside the union of its processors' windows are
-// sorted (with their positions) and each distinct id becomes one entry:
-// bit0 = inside the repetition window, bit1 = inside the presence window,
-// bits 8.. = occurrences inside the frequency window.  Entries are ascending
-// by id, and tile_off[t] is the first entry with id >= t * kTile, so the
-// streaming kernel finds a tile's overrides in O(1).
+// For every row, each distinct id inside the union of its processors'
+// windows becomes one entry: bit0 = inside the repetition window, bit1 =
+// inside the presence window, bits 8.. = occurrences inside the frequency
+// window.  Entries are grouped by 1024-token tile (in no particular order
+// inside a tile), and tile_off[t] is the first entry of tile t, so the
+// streaming kernels find a tile's overrides in O(1).
 //
 // Windows follow Python's tokens[-context_size:] (mlx-lm's processors slice
 // the running sequence that way; reference verify_decode.py:828-831).
@@ -42,11 +42,20 @@ __device__ __forceinline__ int window_start(int H, int ctx) {
   return (-ctx) < H ? -ctx : H;
 }
 
-// one CTA of 1024 threads per row; dynamic shared memory: cap u64 keys, 64 ints, cap ints
+// One CTA of 1024 threads per row.  The ids of the union window go into a
+// shared-memory hash table (open addressing, 2 x cap slots) that keeps each
+// distinct id's latest position and its count inside the frequency window;
+// the entries with an effect are then bucketed by tile (a counting pass and a
+// scatter), in no particular order inside a tile.  Dynamic shared memory:
+// 3 x (2 cap) ints + 2 x 264 ints.
 __global__ void __launch_bounds__(1024) k_prep_overrides(PrepArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);
-  int* wsum = reinterpret_cast<int*>(keys + a.cap);
+  const int slots = 2 * a.cap;
+  int* hid = reinterpret_cast<int*>(smem_raw);
+  int* hlast = hid + slots;
+  int* hcnt = hlast + slots;
+  int* tcount = hcnt + slots;  // [264]
+  int* tcur = tcount + 264;    // [264]
   const int tid = threadIdx.x, nth = blockDim.x;
   const int64_t r = blockIdx.x;
   if (r >= a.rows) return;
@@ -68,139 +77,72 @@ __global__ void __launch_bounds__(1024) k_prep_overrides(PrepArgs a) {
   int n = H - s;
   if (tid == 0) a.status[r] = n > a.cap ? 2 : 0;  // 2: window longer than this build's history cap
   if (n > a.cap) n = 0;
-  // load (id << 32 | position); ids outside [0, V) sort last and are dropped
-  for (int i = tid; i < a.cap; i += nth) {
-    uint64_t k = ~0ull;
-    if (i < n) {
-      const int pos = s + i;
-      const int64_t tok =
-          (int64_t)(pos < Hb ? a.hist[b * a.hist_stride + pos] : a.feed[b * a.feed_group + (pos - Hb)]) - a.id_base;
-      if (tok >= 0 && tok < a.vocab) k = ((uint64_t)(uint32_t)tok << 32) | (uint32_t)pos;
-    }
-    keys[i] = k;
-  }
+  for (int i = tid; i < slots; i += nth) { hid[i] = -1; hlast[i] = -1; hcnt[i] = 0; }
+  for (int i = tid; i < 264; i += nth) tcount[i] = 0;
   __syncthreads();
-  for (int k = 2; k <= a.cap; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < a.cap; i += nth) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint64_t x = keys[i], y = keys[ixj];
-          const bool asc = (i & k) == 0;
-          if (asc ? (x > y) : (x < y)) { keys[i] = y; keys[ixj] = x; }
-        }
+  // insert every position of the window; ids outside [0, V) are dropped
+  for (int i = tid; i < n; i += nth) {
+    const int pos = s + i;
+    const int64_t tok =
+        (int64_t)(pos < Hb ? a.hist[b * a.hist_stride + pos] : a.feed[b * a.feed_group + (pos - Hb)]) - a.id_base;
+    if (tok < 0 || tok >= a.vocab) continue;
+    uint32_t h = ((uint32_t)tok * 2654435761u) % (uint32_t)slots;
+    for (int probe = 0; probe < slots; ++probe) {
+      const int prev = atomicCAS(&hid[h], -1, (int)tok);
+      if (prev == -1 || prev == (int)tok) {
+        atomicMax(&hlast[h], pos);
+        if (freq && pos >= s_freq) atomicAdd(&hcnt[h], 1);
+        break;
       }
-      __syncthreads();
+      h = h + 1 == (uint32_t)slots ? 0u : h + 1;
     }
   }
-  // Runs of equal ids are contiguous and ascending by position.  A run's
-  // last element carries its latest position (the repetition / presence
-  // windows) and, through two block scans, the run's first index and the
-  // number of its positions inside the frequency window.  Each thread owns a
-  // contiguous block of E entries.
-  const int E = a.cap / nth > 0 ? a.cap / nth : 1;
-  const int lo = tid * E;
-  int* fpre = reinterpret_cast<int*>(wsum + 64);  // inclusive count of in-window positions, per entry
-  int fsum = 0, smax = 0;
-  for (int e = 0; e < E; ++e) {
-    const int i = lo + e;
-    if (i >= a.cap) break;
-    const uint64_t k = keys[i];
-    const bool valid = k != ~0ull;
-    if (valid && (i == 0 || (uint32_t)(keys[i - 1] >> 32) != (uint32_t)(k >> 32))) smax = i;
-    fsum += (valid && freq && (int)(uint32_t)k >= s_freq) ? 1 : 0;
+  __syncthreads();
+  // entries with an effect, counted per tile
+  for (int i = tid; i < slots; i += nth) {
+    const int tok = hid[i];
+    if (tok < 0) continue;
+    const int last = hlast[i];
+    const uint32_t info = (rep && last >= s_rep ? 1u : 0u) | (pres && last >= s_pres ? 2u : 0u) |
+                          ((uint32_t)hcnt[i] << 8);
+    hcnt[i] = (int)info;  // reuse the slot for the entry's info
+    if (info) atomicAdd(&tcount[tok / kTile], 1);
   }
-  // block scans: exclusive sum of in-window counts, exclusive max of run starts
-  {
-    const int lane = tid & 31, wid = tid >> 5;
-    int is = fsum, im = smax;  // warp-inclusive
+  __syncthreads();
+  // tile offsets (exclusive prefix over the tiles, one warp)
+  if (tid < 32) {
+    const int per = (a.n_tiles + 1 + 31) / 32;  // <= 9 for 257 entries
+    int loc[9];
+    int sum = 0;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int ts = __shfl_up_sync(kFull, is, o), tm = __shfl_up_sync(kFull, im, o);
-      if (lane >= o) { is += ts; im = max(im, tm); }
+    for (int k = 0; k < 9; ++k) {
+      const int t = tid * per + k;
+      loc[k] = (k < per && t <= a.n_tiles) ? tcount[t] : 0;
+      sum += loc[k];
     }
-    if (lane == 31) { wsum[wid] = is; wsum[32 + wid] = im; }
-    __syncthreads();
-    if (wid == 0) {
-      const int nw2 = nth >> 5;
-      int xs = lane < nw2 ? wsum[lane] : 0, xm = lane < nw2 ? wsum[32 + lane] : 0;
+    const int incl = warp_incl_scan(sum);
+    int run = incl - sum;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int ts = __shfl_up_sync(kFull, xs, o), tm = __shfl_up_sync(kFull, xm, o);
-        if (lane >= o) { xs += ts; xm = max(xm, tm); }
+    for (int k = 0; k < 9; ++k) {
+      const int t = tid * per + k;
+      if (k < per && t <= a.n_tiles) {
+        tcur[t] = run;
+        a.ovr_off[r * (int64_t)(a.n_tiles + 1) + t] = run;
+        run += loc[k];
       }
-      if (lane < nw2) { wsum[lane] = xs; wsum[32 + lane] = xm; }
     }
-    __syncthreads();
-    const int prev_m = __shfl_up_sync(kFull, im, 1);
-    fsum = (is - fsum) + (wid > 0 ? wsum[wid - 1] : 0);
-    smax = max(lane > 0 ? prev_m : 0, wid > 0 ? wsum[32 + wid - 1] : 0);
-  }
-  __syncthreads();  // wsum is reused for the emit scan below
-  int run_start[8];
-  int emit_local = 0;
-  uint32_t info_loc[8];
-  int tok_loc[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) { info_loc[e] = 0; tok_loc[e] = -1; run_start[e] = 0; }
-  for (int e = 0; e < E && e < 8; ++e) {
-    const int i = lo + e;
-    if (i >= a.cap) break;
-    const uint64_t k = keys[i];
-    const bool valid = k != ~0ull;
-    if (valid && (i == 0 || (uint32_t)(keys[i - 1] >> 32) != (uint32_t)(k >> 32))) smax = i;
-    run_start[e] = smax;
-    fsum += (valid && freq && (int)(uint32_t)k >= s_freq) ? 1 : 0;
-    fpre[i] = fsum;
   }
   __syncthreads();
-  for (int e = 0; e < E && e < 8; ++e) {
-    const int i = lo + e;
-    if (i >= a.cap) break;
-    const uint64_t k = keys[i];
-    if (k == ~0ull) continue;
-    const uint32_t tok = (uint32_t)(k >> 32);
-    if (i + 1 < a.cap && keys[i + 1] != ~0ull && (uint32_t)(keys[i + 1] >> 32) == tok) continue;  // not a run end
-    const int last_pos = (int)(uint32_t)k;
-    const int st = run_start[e];
-    uint32_t info = 0;
-    if (rep && last_pos >= s_rep) info |= 1u;
-    if (pres && last_pos >= s_pres) info |= 2u;
-    if (freq) info |= (uint32_t)(fpre[i] - (st > 0 ? fpre[st - 1] : 0)) << 8;
-    if (info) { info_loc[e] = info; tok_loc[e] = (int)tok; ++emit_local; }
-  }
-  // block exclusive scan of emit counts
-  const int lane = tid & 31, wid = tid >> 5;
-  const int incl = warp_incl_scan(emit_local);
-  if (lane == 31) wsum[wid] = incl;
-  __syncthreads();
-  if (wid == 0) {
-    const int v = lane < (nth >> 5) ? wsum[lane] : 0;
-    const int vi = warp_incl_scan(v);
-    if (lane < (nth >> 5)) wsum[lane] = vi - v;
-  }
-  __syncthreads();
-  int pos = wsum[wid] + incl - emit_local;
   int32_t* out_tok = a.ovr_tok + r * a.cap;
   uint32_t* out_info = a.ovr_info + r * a.cap;
-  for (int e = 0; e < E && e < 8; ++e) {
-    if (tok_loc[e] >= 0) { out_tok[pos] = tok_loc[e]; out_info[pos] = info_loc[e]; ++pos; }
-  }
-  __syncthreads();
-  // total count = exclusive start of the last thread + its count
-  __shared__ int total_s;
-  if (tid == nth - 1) total_s = pos;
-  __syncthreads();
-  const int total = total_s;
-  // tile offsets: lower_bound over the emitted ids (read back from global)
-  for (int t = tid; t <= a.n_tiles; t += nth) {
-    const int64_t key = (int64_t)t * kTile;
-    int lo3 = 0, hi3 = total;
-    while (lo3 < hi3) {
-      const int mid = (lo3 + hi3) >> 1;
-      if ((int64_t)out_tok[mid] >= key) hi3 = mid; else lo3 = mid + 1;
-    }
-    a.ovr_off[r * (int64_t)(a.n_tiles + 1) + t] = lo3;
+  for (int i = tid; i < slots; i += nth) {
+    const int tok = hid[i];
+    if (tok < 0) continue;
+    const uint32_t info = (uint32_t)hcnt[i];
+    if (!info) continue;
+    const int at = atomicAdd(&tcur[tok / kTile], 1);
+    out_tok[at] = tok;
+    out_info[at] = info;
   }
 }
 

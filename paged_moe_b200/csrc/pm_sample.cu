@@ -43,6 +43,10 @@ struct PartState {
   Cand cd;
   bool published;   // a compaction raised the threshold since the last publish
   uint64_t rtau;    // the row's shared threshold, loaded one tile ahead
+  // min-p without top-k / top-p (and min_tokens_to_keep <= 1): nothing below
+  // (part maximum) + log(min_p) - 1 can survive, so offers start there
+  bool minp_floor;
+  float floor;
 };
 
 __device__ __forceinline__ void part_begin(const SampleArgs& a, int64_t row, int first_tile, int KC,
@@ -57,6 +61,9 @@ __device__ __forceinline__ void part_begin(const SampleArgs& a, int64_t row, int
   cand_reset(ps.cd);
   ps.published = false;
   ps.rtau = 0;
+  ps.minp_floor = (ps.p.flags & PM_F_MIN_P) && !(ps.p.flags & PM_F_TOP_P) && ps.p.top_k <= 0 &&
+                  ps.p.min_tokens_to_keep <= 1;
+  ps.floor = -INFINITY;
 }
 
 // Share the part's threshold with the other parts of the row, and adopt
@@ -285,6 +292,8 @@ __device__ __forceinline__ void scan_tile_masked(const SampleArgs& a, int64_t ro
   __syncwarp();
   if (ps.needx) {
     const float m = warp_max(mx);
+    if (MODE == kCand && ps.minp_floor && m > -INFINITY)
+      ps.floor = fmaxf(ps.floor, fsub(fadd(m, ps.p.log_min_p), 1.0f));
     uint64_t sum = 0;
     if (m > -INFINITY) sum = sum_compacted<2>(buf, base, m, inv_t);
     sum = warp_sum_u64(sum);
@@ -314,6 +323,8 @@ __device__ __forceinline__ void scan_tile_mode(const SampleArgs& a, int64_t row,
   scan_pass<S, 1, MODE, KC>(buf, dense, slots, start, 0.0f, inv_t, ps, acc, wm);
   if (ps.needx) {
     const float m = warp_max(acc.mx);
+    if (MODE == kCand && ps.minp_floor && m > -INFINITY)
+      ps.floor = fmaxf(ps.floor, fsub(fadd(m, ps.p.log_min_p), 1.0f));
     if (m > -INFINITY) scan_pass<S, 2, MODE, KC>(buf, dense, slots, start, m, inv_t, ps, acc, wm);
     const uint64_t sum = warp_sum_u64(acc.sx);
     if (lane == 0) { TileStat t; t.m = m; t.pad = 0; t.s = sum; a.statx[row * a.n_tiles + tile] = t; }
@@ -446,18 +457,44 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
       continue;
     }
     const int K = (p.top_k > 0 && p.top_k < KC) ? p.top_k : KC;
-    // 1. each warp: parts wid, wid + 8, ... into its own top-K
+    // 1. each warp: parts wid, wid + 8, ... into its own top-K; a round takes
+    //    32 of the warp's parts at once (lane i: part wid + 8 (p0 + i)), their
+    //    keys flattened and loaded eight per lane in flight
     {
       Cand cd;
       cand_reset(cd);
       bool trimmed = false;
-      for (int part = wid; part < n_parts; part += 8) {
-        const int raw = ld_cg(&a.cand_n[row * a.max_parts + part]);
-        trimmed |= ((raw >> 30) & 1) != 0;
+      const int mine_n = n_parts > wid ? (n_parts - wid + 7) / 8 : 0;
+      for (int p0 = 0; p0 < mine_n; p0 += 32) {
+        const int part = wid + 8 * (p0 + lane);
+        const int raw = p0 + lane < mine_n ? ld_cg(&a.cand_n[row * a.max_parts + part]) : 0;
+        trimmed |= __any_sync(kFull, (raw >> 30) & 1) != 0;
         const int n = raw & 0x3fffffff;
-        const uint64_t* src = a.cand + (row * a.max_parts + part) * (int64_t)KC;
-        for (int i0 = 0; i0 < n; i0 += 32)
-          cand_offer_key<CAP>(i0 + lane < n ? ld_cg(&src[i0 + lane]) : 0ull, mc->cand[wid], mc->hist[wid], cd, K);
+        const int incl = warp_incl_scan(n);
+        const int tot = __shfl_sync(kFull, incl, 31);
+        for (int f0 = 0; f0 < tot; f0 += 256) {
+          uint64_t keys[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int f = f0 + u * 32 + lane;
+            int q = 0;  // lanes whose inclusive prefix is <= f
+#pragma unroll
+            for (int st = 16; st > 0; st >>= 1) {
+              const int v = __shfl_sync(kFull, incl, (q + st - 1) & 31);
+              if (q + st - 1 < 32 && v <= f) q += st;
+            }
+            const int qi = q < 32 ? q : 31;
+            const int iq = __shfl_sync(kFull, incl, qi);
+            const int nq = __shfl_sync(kFull, n, qi);
+            keys[u] = 0ull;
+            if (f < tot) {
+              const uint64_t* src = a.cand + (row * a.max_parts + wid + 8 * (p0 + qi)) * (int64_t)KC;
+              keys[u] = ld_cg(&src[f - (iq - nq)]);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) cand_offer_key<CAP>(keys[u], mc->cand[wid], mc->hist[wid], cd, K);
+        }
       }
       if (cd.cnt > K) cand_compact<CAP>(mc->cand[wid], mc->hist[wid], cd, K);
       for (int i = lane; i < cd.cnt; i += 32) mc->u[wid * KC + i] = mc->cand[wid][i];
@@ -600,7 +637,10 @@ __global__ void __launch_bounds__(kThreadsS, 3) k_sample_stream(const __grid_con
       oe = off[1];
     }
     if (a.bias_off) { bb = a.bias_off[tile]; be = a.bias_off[tile + 1]; }
-    if (ps.mode == kCand) share_threshold(a, row, ps);
+    if (ps.mode == kCand) {
+      share_threshold(a, row, ps);
+      if (ps.floor > ps.cd.tau_x) ps.cd.tau_x = ps.floor;
+    }
     if (oe > ob || be > bb) {
       if constexpr (sizeof(T) == 2) expand_bf16_in_place(buf);
       apply_overrides_smem(a, ps.p, row, tile, ob, oe, bb, be, buf);
@@ -884,10 +924,10 @@ int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::Sample
     pa.ovr_info = reinterpret_cast<uint32_t*>(ws + L.ovr_info);
     pa.ovr_off = reinterpret_cast<int32_t*>(ws + L.ovr_off);
     pa.status = a.status;
-    const size_t smem = sizeof(uint64_t) * L.ovr_cap + 64 * sizeof(int) + sizeof(int) * L.ovr_cap;
+    const size_t smem = sizeof(int) * (6 * (size_t)L.ovr_cap + 2 * 264);
     static std::once_flag once;
     std::call_once(once, [] {
-      cudaFuncSetAttribute(pm::k_prep_overrides, cudaFuncAttributeMaxDynamicSharedMemorySize, 8192 * 12 + 256);
+      cudaFuncSetAttribute(pm::k_prep_overrides, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * (6 * 8192 + 2 * 264));
     });
     pm::k_prep_overrides<<<(unsigned)r->rows, 1024, smem, st>>>(pa);
     e = cudaGetLastError();
