@@ -22,7 +22,10 @@ constexpr int kStages = 3;
 // Per-warp shared memory of the streaming kernels.
 template <int KC>
 struct alignas(128) StreamMem {
-  static constexpr int CAP = KC + 384;  // KC kept + room for several push rounds between compactions
+  // KC kept + room for several push rounds between compactions.  The extra
+  // room for KC = 64 still fits three 4-warp CTAs per SM; KC = 256 keeps
+  // +384 for the same reason.
+  static constexpr int CAP = KC == 64 ? KC + 576 : KC + 384;
   float tile[kStages][kTile];           // fp32 tile, or a bf16 tile in the first half
   uint32_t mask[kStages][32];
   uint64_t bar[kStages];
