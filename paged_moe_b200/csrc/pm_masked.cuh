@@ -31,6 +31,8 @@ constexpr int kWin = 4096;                          // allowed tokens per window
 constexpr int kMaxTiles = 32 * kMaxPer;             // tiles of the largest row (256)
 constexpr int kMaxWords = kMaxTiles * 32;           // mask words of the largest row (8192)
 constexpr int kSel = 1024;                          // keys the fast selection path holds
+constexpr int kRun = kWin / kMThreads;              // positions a thread owns in a window (16)
+static_assert(kMThreads == kMaxTiles && kMWarps == 8, "the row log-sum-exp gives one tile per thread, 8 warps");
 
 template <int KC>
 struct MaskedMem {
@@ -48,10 +50,12 @@ struct MaskedMem {
   unsigned hist[256];
   int scal[8];
   uint64_t wbest[kMWarps];
+  uint32_t rmx[kMThreads];    // each thread's run maximum (ordered key; 0: nothing finite)
+  double redd[kMWarps];       // per-warp subtrees of the log-sum-exp
+  float redf[kMWarps];
   float score[KC];            // Gumbel scores of the carried keys
   int nsel;
   float v0;
-  float lse;
 };
 
 __device__ __forceinline__ float ord_value(uint32_t o) {
@@ -84,6 +88,17 @@ __device__ __forceinline__ uint64_t seg_sum_u64(uint64_t v, int seg) {
 __device__ __forceinline__ bool seg_head(int seg) {
   const int prev = __shfl_up_sync(kFull, seg, 1);
   return (threadIdx.x & 31) == 0 || prev != seg;
+}
+
+// dst += v for a 64-bit shared-memory counter, as two native 32-bit atomic
+// adds: the carry out of the low word is read from the value it held.  Exact
+// while the high word does not overflow.
+__device__ __forceinline__ void smem_add_u64(uint64_t* dst, uint64_t v) {
+  uint32_t* w = reinterpret_cast<uint32_t*>(dst);
+  const uint32_t lo = (uint32_t)v;
+  const uint32_t old = atomicAdd(&w[0], lo);
+  const uint32_t hi = (uint32_t)(v >> 32) + (old + lo < old ? 1u : 0u);
+  if (hi) atomicAdd(&w[1], hi);
 }
 
 __device__ __forceinline__ void cp_async4(void* dst, const void* src, uint64_t policy) {
@@ -184,20 +199,29 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
       const int w = tid + k * kMThreads;
       wr[k] = (k < KW && w < nw) ? __ldcs(mrow + w) : 0u;
     }
+    // groups of four rounds without a branch between them, so their warp
+    // scans overlap; rounds past the row write zero counts into slots that
+    // exist (kMaxWords words, kMaxTiles tiles) and nothing reads
 #pragma unroll
-    for (int k = 0; k < kMaxPer * 4; ++k) {
-      const int w = tid + k * kMThreads;
-      const int tile = k * kMWarps + wid;
-      if (k < KW && tile < nt) {  // warp-uniform
+    for (int k0 = 0; k0 < kMaxPer * 4; k0 += 4) {
+      if (k0 >= KW) break;  // CTA-uniform
+#pragma unroll
+      for (int k = k0; k < k0 + 4; ++k) {
+        const int w = tid + k * kMThreads;
         uint32_t word = wr[k];
         if (w == nw - 1 && (a.vocab & 31)) word &= (1u << (a.vocab & 31)) - 1u;
         mm->mw[w] = word;
         const int pc = __popc(word);
         const int incl = warp_incl_scan(pc);
         mm->wpre[w] = (uint16_t)(incl - pc);
-        if (lane == 31) mm->toff[tile + 1] = incl;
+        if (lane == 31) mm->toff[k * kMWarps + wid + 1] = incl;
       }
     }
+    // tile statistics start at zero (each window fills its own tiles)
+    mm->tmx[tid] = 0;
+    mm->tmy[tid] = 0;
+    mm->tsx[tid] = 0;
+    mm->tsy[tid] = 0;
     __syncthreads();
     if (wid == 0) {
       int c[kMaxPer];
@@ -283,67 +307,86 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
         }
         __syncthreads();
       }
-      for (int t = t0 + tid; t < t1; t += kMThreads) {
-        mm->tmx[t] = 0;
-        mm->tmy[t] = 0;
-        mm->tsx[t] = 0;
-        mm->tsy[t] = 0;
-      }
-      __syncthreads();
-      // each lane owns a contiguous run of positions (tiles are runs of positions)
+      // each thread owns a contiguous run of at most kRun positions (tiles are
+      // runs of positions), held in registers: values and token ids
       const int rl = (n + kMThreads - 1) / kMThreads;
-      const int q0 = min(n, tid * rl), q1 = min(n, q0 + rl);
-      // exact tile statistics: maxima, then q52 sums against them
+      const int q0 = min(n, tid * rl);
+      const int len = min(n, q0 + rl) - q0;
+      float xv[kRun];
+      uint32_t iv[kRun];
+#pragma unroll
+      for (int r = 0; r < kRun; ++r) {
+        xv[r] = r < len ? vf(q0 + r) : -INFINITY;
+        iv[r] = r < len ? mm->ids[q0 + r] : 0u;
+      }
+      // exact tile statistics: maxima, then q52 sums against them; a run's
+      // tiles are flushed to shared memory when the tile changes
       if (want_max) {
-        int cur = -1;
-        uint32_t mx = 0, my = 0;
-        for (int i = q0; i < q1; ++i) {
-          const float x = vf(i);
-          const int seg = (int)(mm->ids[i] >> 10);
-          if (seg != cur) {
-            if (cur >= 0) {
+        int cur = (int)(iv[0] >> 10);
+        uint32_t mx = 0, my = 0, rmax = 0;
+#pragma unroll
+        for (int r = 0; r < kRun; ++r) {
+          if (r < len) {
+            const int seg = (int)(iv[r] >> 10);
+            if (seg != cur) {
               if (mx) atomicMax(&mm->tmx[cur], mx);
               if (my) atomicMax(&mm->tmy[cur], my);
+              cur = seg;
+              mx = my = 0;
             }
-            cur = seg;
-            mx = my = 0;
-          }
-          if (x > -INFINITY) {
-            mx = max(mx, ordkey(x));
-            if (needy) my = max(my, ordkey(fmul(x, inv_t)));
+            if (xv[r] > -INFINITY) {
+              mx = max(mx, ordkey(xv[r]));
+              rmax = max(rmax, ordkey(xv[r]));
+              if (needy) my = max(my, ordkey(fmul(xv[r], inv_t)));
+            }
           }
         }
-        if (cur >= 0) {
+        if (len > 0) {
           if (mx) atomicMax(&mm->tmx[cur], mx);
           if (my) atomicMax(&mm->tmy[cur], my);
         }
+        mm->rmx[tid] = rmax;
         __syncthreads();
       }
       if (needx || needy) {
-        int cur = -1;
+        // q52 of -inf or NaN is 0: positions past the run and tiles with
+        // nothing finite add nothing
+        auto tile_m = [](uint32_t o) { return o ? ord_value(o) : -INFINITY; };
+        int cur = (int)(iv[0] >> 10);
         uint64_t sx = 0, sy = 0;
-        float mxv = -INFINITY, myv = -INFINITY;
-        for (int i = q0; i < q1; ++i) {
-          const float x = vf(i);
-          const int seg = (int)(mm->ids[i] >> 10);
-          if (seg != cur) {
-            if (cur >= 0) {
-              if (sx) atomicAdd(reinterpret_cast<unsigned long long*>(&mm->tsx[cur]), (unsigned long long)sx);
-              if (sy) atomicAdd(reinterpret_cast<unsigned long long*>(&mm->tsy[cur]), (unsigned long long)sy);
-            }
-            cur = seg;
-            sx = sy = 0;
-            mxv = mm->tmx[seg] ? ord_value(mm->tmx[seg]) : -INFINITY;
-            myv = mm->tmy[seg] ? ord_value(mm->tmy[seg]) : -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kRun; r += 2) {
+          uint64_t qx0 = 0, qx1 = 0, qy0 = 0, qy1 = 0;
+          const uint32_t s0 = iv[r] >> 10, s1 = iv[r + 1] >> 10;
+          if (needx) {
+            const float d0 = r < len ? fsub(xv[r], tile_m(mm->tmx[s0])) : -INFINITY;
+            const float d1 = r + 1 < len ? fsub(xv[r + 1], tile_m(mm->tmx[s1])) : -INFINITY;
+            q52x2(d0, d1, qx0, qx1);
           }
-          if (x > -INFINITY) {
-            if (needx && mxv > -INFINITY) sx += q52(fsub(x, mxv));
-            if (needy && myv > -INFINITY) sy += q52(fsub(fmul(x, inv_t), myv));
+          if (needy) {
+            const float d0 = r < len && xv[r] > -INFINITY ? fsub(fmul(xv[r], inv_t), tile_m(mm->tmy[s0])) : -INFINITY;
+            const float d1 = r + 1 < len && xv[r + 1] > -INFINITY
+                                 ? fsub(fmul(xv[r + 1], inv_t), tile_m(mm->tmy[s1])) : -INFINITY;
+            q52x2(d0, d1, qy0, qy1);
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (r + h < len) {
+              const int seg = (int)(h ? s1 : s0);
+              if (seg != cur) {
+                if (sx) smem_add_u64(&mm->tsx[cur], sx);
+                if (sy) smem_add_u64(&mm->tsy[cur], sy);
+                cur = seg;
+                sx = sy = 0;
+              }
+              sx += h ? qx1 : qx0;
+              sy += h ? qy1 : qy0;
+            }
           }
         }
-        if (cur >= 0) {
-          if (sx) atomicAdd(reinterpret_cast<unsigned long long*>(&mm->tsx[cur]), (unsigned long long)sx);
-          if (sy) atomicAdd(reinterpret_cast<unsigned long long*>(&mm->tsy[cur]), (unsigned long long)sy);
+        if (len > 0) {
+          if (sx) smem_add_u64(&mm->tsx[cur], sx);
+          if (sy) smem_add_u64(&mm->tsy[cur], sy);
         }
         __syncthreads();
         for (int t = t0 + tid; t < t1; t += kMThreads) {
@@ -364,10 +407,10 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
       // selection
       if (mode == kGreedy) {
         uint64_t b = 0;
-        for (int i = tid; i < n; i += kMThreads) {
-          const float x = vf(i);
-          const uint64_t k = rankkey(x, mm->ids[i]);
-          if (x > -INFINITY && k > b) b = k;  // nothing finite at all: token 0, as the streaming pass
+#pragma unroll
+        for (int r = 0; r < kRun; ++r) {
+          const uint64_t k = rankkey(xv[r], iv[r]);
+          if (r < len && xv[r] > -INFINITY && k > b) b = k;  // nothing finite at all: token 0, as the streaming pass
         }
         b = warp_max_u64(b);
         if (lane == 0) mm->wbest[wid] = b;
@@ -375,32 +418,54 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
 #pragma unroll
         for (int w = 0; w < kMWarps; ++w) best = mm->wbest[w] > best ? mm->wbest[w] : best;
       } else if (mode == kCand) {
-        // v0: the K-th largest finite tile maximum of the window bounds its top-K
-        // from below (at least K tokens reach it); found by counting ranks
-        const int ntw = t1 - t0;  // <= 256 = threads
-        uint64_t tk = 0;
-        if (tid < ntw) {
-          const uint32_t v = mm->tmx[t0 + tid];
-          tk = v ? (((uint64_t)v << 32) | (uint32_t)tid) : 0ull;
-          mm->sel[tid] = tk;
-        }
-        if (tid == 0) { mm->v0 = -INFINITY; mm->nsel = 0; }
-        __syncthreads();
-        if (tk) {
-          int rank = 0;
-          for (int t = 0; t < ntw; ++t) rank += mm->sel[t] > tk;
-          if (rank == K - 1) mm->v0 = ord_value((uint32_t)(tk >> 32));
+        // v0: the K-th largest of the threads' run maxima bounds the window's
+        // top-K from below (K distinct tokens reach it); the K-th largest of
+        // their upper 16 key bits, padded with zero bits, still does.  Warp 0
+        // finds it two bits at a time: the largest T with at least K run
+        // maxima >= T.
+        if (wid == 0) {
+          uint32_t rv[kMThreads / 32];
+#pragma unroll
+          for (int j = 0; j < kMThreads / 32; ++j) rv[j] = mm->rmx[lane + 32 * j] >> 16;
+          uint32_t T = 0;
+#pragma unroll
+          for (int b = 14; b >= 0; b -= 2) {
+            unsigned n1 = 0, n2 = 0, n3 = 0;
+#pragma unroll
+            for (int j = 0; j < kMThreads / 32; ++j) {
+              n1 += rv[j] >= (T | (1u << b)) ? 1u : 0u;
+              n2 += rv[j] >= (T | (2u << b)) ? 1u : 0u;
+              n3 += rv[j] >= (T | (3u << b)) ? 1u : 0u;
+            }
+            const uint32_t d = ((int)__reduce_add_sync(kFull, n1) >= K ? 1u : 0u) +
+                               ((int)__reduce_add_sync(kFull, n2) >= K ? 1u : 0u) +
+                               ((int)__reduce_add_sync(kFull, n3) >= K ? 1u : 0u);
+            T |= d << b;
+          }
+          if (lane == 0) {
+            mm->v0 = T ? ord_value(T << 16) : -INFINITY;
+            mm->nsel = 0;
+          }
         }
         __syncthreads();
         const float v0 = mm->v0;
         // keys of the window that can still enter the top-K
-        for (int i = q0; i < q1; ++i) {
-          const float x = vf(i);
-          if (!(x > -INFINITY) || x < v0) continue;
-          const uint64_t k = rankkey(x, mm->ids[i]);
-          if (k <= tau) continue;
-          const int at = atomicAdd(&mm->nsel, 1);
-          if (at < kSel) mm->sel[at] = k;
+        {
+          uint32_t okm = 0;
+#pragma unroll
+          for (int r = 0; r < kRun; ++r)
+            if (r < len && xv[r] > -INFINITY && xv[r] >= v0 && rankkey(xv[r], iv[r]) > tau) okm |= 1u << r;
+          const int c = __popc(okm);
+          const int incl = warp_incl_scan(c);
+          int at = 0;
+          if (lane == 31 && incl) at = atomicAdd(&mm->nsel, incl);
+          at = __shfl_sync(kFull, at, 31) + incl - c;
+#pragma unroll
+          for (int r = 0; r < kRun; ++r)
+            if ((okm >> r) & 1u) {
+              if (at < kSel) mm->sel[at] = rankkey(xv[r], iv[r]);
+              ++at;
+            }
         }
         __syncthreads();
         const int ns = mm->nsel;
@@ -414,6 +479,7 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
             for (int i = tid; i < total; i += kMThreads) {
               const uint64_t k = mm->sel[i];
               int rank = 0;
+#pragma unroll 8
               for (int j = 0; j < total; ++j) rank += mm->sel[j] > k;
               if (rank < K) mm->carry[rank] = k;
             }
@@ -484,30 +550,43 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
       __syncthreads();
       t0 = t1;
     }
-    // 3. the draw: log-sum-exp (warp 0) and the carried keys' Gumbel scores
-    //    (every other thread) side by side, then filters and draw (warp 0)
-    if (wid == 0 && needx) {
-      LaneTiles lt;
-      int P = 32;
-      while (P < nt) P <<= 1;
-      lt.per = P >> 5;
-      lt.nt = nt;
+    // 3. the draw.  Log-sum-exp by the whole CTA: thread t weighs tile t
+    //    (kMThreads = kMaxTiles), each warp sums its 32 tiles pairwise, and
+    //    the eight warp sums close the same zero-padded 256-leaf pairwise tree
+    //    as the one-warp combine (every warp subtree is one of its subtrees),
+    //    so the bits agree.  The carried keys' Gumbel scores meanwhile.
+    float m_row = -INFINITY;
+    if (needx) {
+      const bool ok = tid < nt && mm->tmx[tid] != 0;
+      const float mt = ok ? ord_value(mm->tmx[tid]) : -INFINITY;
+      const uint64_t st = ok ? mm->tsx[tid] : 0ull;
+      const float wmx = warp_max(mt);
+      if (lane == 0) mm->redf[wid] = wmx;
+      __syncthreads();
 #pragma unroll
-      for (int i = 0; i < kMaxPer; ++i) {
-        const int t = lane * lt.per + i;
-        const bool ok = i < lt.per && t < nt && mm->tmx[t] != 0;
-        lt.m[i] = ok ? ord_value(mm->tmx[t]) : -INFINITY;
-        lt.s[i] = ok ? mm->tsx[t] : 0ull;
+      for (int w = 0; w < kMWarps; ++w) m_row = fmaxf(m_row, mm->redf[w]);
+      double v = m_row > -INFINITY ? tile_weight_of(mt, st, m_row) : 0.0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double t = __shfl_down_sync(kFull, v, o);
+        if ((lane & (2 * o - 1)) == 0) v = dadd(v, t);
       }
-      const float cc = combine_lane_tiles(lt, lane_tiles_max(lt));
-      if (lane == 0) mm->lse = cc;
+      if (lane == 0) mm->redd[wid] = v;
     }
     if (mode == kCand)
-      for (int r = tid - 32; r >= 0 && r < ncarry; r += kMThreads - 32)
+      for (int r = tid; r < ncarry; r += kMThreads)
         mm->score[r] = fadd(fmul(key_value(mm->carry[r]), inv_t), row_gumbel(a, row, key_index(mm->carry[r])));
     __syncthreads();
     if (wid == 0) {
-      const float c = needx ? mm->lse : __int_as_float(0x7fc00000);
+      float c = __int_as_float(0x7fc00000);
+      if (needx) {
+        c = -INFINITY;
+        if (m_row > -INFINITY) {
+          const double z = dadd(dadd(dadd(mm->redd[0], mm->redd[1]), dadd(mm->redd[2], mm->redd[3])),
+                                dadd(dadd(mm->redd[4], mm->redd[5]), dadd(mm->redd[6], mm->redd[7])));
+          c = (float)dadd((double)m_row, det_log64(dmul(z, 0x1p-52)));
+        }
+      }
       int tok = 0, ns = 0;
       float x_tok = -INFINITY;
       if (mode == kGreedy) {

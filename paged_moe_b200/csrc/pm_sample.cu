@@ -639,7 +639,18 @@ __global__ void __launch_bounds__(kThreadsS, 3) k_sample_stream(const __grid_con
     if (a.bias_off) { bb = a.bias_off[tile]; be = a.bias_off[tile + 1]; }
     if (ps.mode == kCand) {
       share_threshold(a, row, ps);
-      if (ps.floor > ps.cd.tau_x) ps.cd.tau_x = ps.floor;
+      // the min-p floor as a key threshold, published like a compaction's:
+      // every part's floor lies below the row's min-p cut, so the largest
+      // one serves all parts of the row
+      if (ps.floor > ps.cd.tau_x) {
+        const uint64_t fk = (uint64_t)ordkey(ps.floor) << 32;
+        if (fk > ps.cd.tau) {
+          ps.cd.tau = fk;
+          ps.cd.tau_x = key_value(fk);
+          ps.cd.trimmed = true;
+          ps.published = true;
+        }
+      }
     }
     if (oe > ob || be > bb) {
       if constexpr (sizeof(T) == 2) expand_bf16_in_place(buf);

@@ -175,6 +175,8 @@ __device__ __forceinline__ double tile_weight_of(float mt, uint64_t s, float m) 
 //   with zeros to a power of two; lane L sums its contiguous block of P/32
 //   tiles as a complete subtree, then the lanes combine pairwise),
 //   c = fl32(m + log(Z 2^-52)).  -inf when no tile has a finite value.
+// kFullPer: lt.per is kMaxPer (no branch on it).
+template <bool kFullPer = false>
 __device__ __forceinline__ float combine_lane_tiles(const LaneTiles& lt, float m) {
   const int lane = threadIdx.x & 31;
   if (!(m > -INFINITY)) return -INFINITY;
@@ -182,7 +184,7 @@ __device__ __forceinline__ float combine_lane_tiles(const LaneTiles& lt, float m
   int sp = 0;
 #pragma unroll
   for (int i = 0; i < kMaxPer; ++i) {
-    if (i < lt.per) {
+    if (kFullPer || i < lt.per) {
       double v = tile_weight_of(lt.m[i], lt.s[i], m);
       for (int c = i + 1; (c & 1) == 0; c >>= 1) v = dadd(stk[--sp], v);
       stk[sp++] = v;
@@ -198,12 +200,23 @@ __device__ __forceinline__ float combine_lane_tiles(const LaneTiles& lt, float m
   return (float)dadd((double)m, det_log64(dmul(Z, 0x1p-52)));
 }
 
+// Every lane takes kMaxPer tiles: the zero-padded 256-leaf pairwise tree
+// sums to the same bits as the tree over the row's own power of two (its
+// right part is exactly zero), with no branch on the tile count.
 __device__ __forceinline__ float warp_combine(const TileStat* st, int nt, float* m_out) {
+  const int lane = threadIdx.x & 31;
   LaneTiles lt;
-  load_lane_tiles(st, nt, lt);
+  lt.per = kMaxPer;
+  lt.nt = nt;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int t = lane * kMaxPer + i;
+    lt.m[i] = t < nt ? ld_cg(&st[t].m) : -INFINITY;
+    lt.s[i] = t < nt ? ld_cg(&st[t].s) : 0ull;
+  }
   const float m = lane_tiles_max(lt);
   *m_out = m;
-  return combine_lane_tiles(lt, m);
+  return combine_lane_tiles<true>(lt, m);
 }
 
 __device__ __forceinline__ float row_gumbel(const SampleArgs& a, int64_t row, uint32_t token) {
