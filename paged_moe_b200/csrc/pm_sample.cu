@@ -82,6 +82,21 @@ __device__ __forceinline__ void share_threshold(const SampleArgs& a, int64_t row
   }
 }
 
+// The min-p floor as a key threshold, published like a compaction's: every
+// part's floor lies below the row's min-p cut, so the largest one serves all
+// parts of the row.
+__device__ __forceinline__ void raise_to_floor(PartState& ps) {
+  if (ps.floor > ps.cd.tau_x) {
+    const uint64_t fk = (uint64_t)ordkey(ps.floor) << 32;
+    if (fk > ps.cd.tau) {
+      ps.cd.tau = fk;
+      ps.cd.tau_x = key_value(fk);
+      ps.cd.trimmed = true;
+      ps.published = true;
+    }
+  }
+}
+
 // Fill stage s of the warp's ring with tile gi by bulk copies (lane 0), when
 // the tile is whole and aligned; returns whether it did (warp-uniform).
 template <typename T, int KC>
@@ -320,6 +335,61 @@ __device__ __forceinline__ void scan_tile_mode(const SampleArgs& a, int64_t row,
   acc.my = -INFINITY;
   acc.sx = 0;
   acc.sy = 0;
+  if (MODE == kCand && dense && ps.minp_floor) {
+    // min-p rows: the tile's own maximum raises the floor before its offers
+    constexpr int VW = Vec<S>::VW;
+    float lm = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 32 / VW; ++j) {
+      float x[VW];
+      read_step<S>(buf, j, lane, x);
+#pragma unroll
+      for (int c = 0; c < VW; ++c) lm = fmaxf(lm, x[c]);
+    }
+    const float m = warp_max(lm);
+    if (m > -INFINITY) {
+      ps.floor = fmaxf(ps.floor, fsub(fadd(m, ps.p.log_min_p), 1.0f));
+      raise_to_floor(ps);
+    }
+  }
+  if (MODE == kCand && dense && ps.cd.tau == 0 && ps.K <= 64) {
+    // the part's first offers: the K-th largest of the tile's 64 half-lane
+    // maxima (16 values each) bounds the part's K-th largest value from
+    // below, and so does its upper 16 key bits padded with zeros; the offers
+    // start there instead of at nothing.  Warp search, two bits a step.
+    constexpr int VW = Vec<S>::VW;
+    float h0 = -INFINITY, h1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 32 / VW; ++j) {
+      float x[VW];
+      read_step<S>(buf, j, lane, x);
+#pragma unroll
+      for (int c = 0; c < VW; ++c) {
+        if (j < 16 / VW) h0 = fmaxf(h0, x[c]);
+        else h1 = fmaxf(h1, x[c]);
+      }
+    }
+    const uint32_t k0 = h0 > -INFINITY ? ordkey(h0) >> 16 : 0u;
+    const uint32_t k1 = h1 > -INFINITY ? ordkey(h1) >> 16 : 0u;
+    uint32_t T = 0;
+#pragma unroll
+    for (int b = 14; b >= 0; b -= 2) {
+      const uint32_t c1 = T | (1u << b), c2 = T | (2u << b), c3 = T | (3u << b);
+      const unsigned n1 = (k0 >= c1 ? 1u : 0u) + (k1 >= c1 ? 1u : 0u);
+      const unsigned n2 = (k0 >= c2 ? 1u : 0u) + (k1 >= c2 ? 1u : 0u);
+      const unsigned n3 = (k0 >= c3 ? 1u : 0u) + (k1 >= c3 ? 1u : 0u);
+      const uint32_t d = ((int)__reduce_add_sync(kFull, n1) >= ps.K ? 1u : 0u) +
+                         ((int)__reduce_add_sync(kFull, n2) >= ps.K ? 1u : 0u) +
+                         ((int)__reduce_add_sync(kFull, n3) >= ps.K ? 1u : 0u);
+      T |= d << b;
+    }
+    if (T) {
+      ps.cd.tau = (uint64_t)(T << 16) << 32;
+      ps.cd.tau_x = key_value(ps.cd.tau);
+      ps.cd.trimmed = true;
+      ps.published = true;
+    }
+  }
   scan_pass<S, 1, MODE, KC>(buf, dense, slots, start, 0.0f, inv_t, ps, acc, wm);
   if (ps.needx) {
     const float m = warp_max(acc.mx);
@@ -639,18 +709,7 @@ __global__ void __launch_bounds__(kThreadsS, 3) k_sample_stream(const __grid_con
     if (a.bias_off) { bb = a.bias_off[tile]; be = a.bias_off[tile + 1]; }
     if (ps.mode == kCand) {
       share_threshold(a, row, ps);
-      // the min-p floor as a key threshold, published like a compaction's:
-      // every part's floor lies below the row's min-p cut, so the largest
-      // one serves all parts of the row
-      if (ps.floor > ps.cd.tau_x) {
-        const uint64_t fk = (uint64_t)ordkey(ps.floor) << 32;
-        if (fk > ps.cd.tau) {
-          ps.cd.tau = fk;
-          ps.cd.tau_x = key_value(fk);
-          ps.cd.trimmed = true;
-          ps.published = true;
-        }
-      }
+      raise_to_floor(ps);
     }
     if (oe > ob || be > bb) {
       if constexpr (sizeof(T) == 2) expand_bf16_in_place(buf);
