@@ -47,6 +47,7 @@ struct PartState {
   // (part maximum) + log(min_p) - 1 can survive, so offers start there
   bool minp_floor;
   float floor;
+  uint64_t fkey;    // the floor as a key (what these rows publish)
 };
 
 __device__ __forceinline__ void part_begin(const SampleArgs& a, int64_t row, int first_tile, int KC,
@@ -61,24 +62,30 @@ __device__ __forceinline__ void part_begin(const SampleArgs& a, int64_t row, int
   cand_reset(ps.cd);
   ps.published = false;
   ps.rtau = 0;
-  ps.minp_floor = (ps.p.flags & PM_F_MIN_P) && !(ps.p.flags & PM_F_TOP_P) && ps.p.top_k <= 0 &&
-                  ps.p.min_tokens_to_keep <= 1;
+  ps.minp_floor = minp_floor_row(ps.p);
   ps.floor = -INFINITY;
+  ps.fkey = 0;
 }
 
+// The threshold a part shares with the other parts of its row: the K-th
+// largest key it holds (a lower bound for the row's K-th largest key), or,
+// on min-p floor rows, its floor.
+__device__ __forceinline__ uint64_t part_bound(const PartState& ps) { return ps.minp_floor ? ps.fkey : ps.cd.tau; }
+
 // Share the part's threshold with the other parts of the row, and adopt
-// theirs: the K-th largest key a part holds is a lower bound for the row's
-// K-th largest key, so keys at or below the largest such bound can never be
-// selected.  Dropping them makes the part's list incomplete ("trimmed").
+// theirs: keys at or below the largest bound can never be selected.
+// Dropping them makes the part's list incomplete ("trimmed"), except below a
+// min-p floor, where the list still holds every survivor.
 __device__ __forceinline__ void share_threshold(const SampleArgs& a, int64_t row, PartState& ps) {
   if (ps.published) {
-    if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<unsigned long long*>(&a.row_tau[row]), ps.cd.tau);
+    const uint64_t b = part_bound(ps);
+    if ((threadIdx.x & 31) == 0 && b) atomicMax(reinterpret_cast<unsigned long long*>(&a.row_tau[row]), b);
     ps.published = false;
   }
   if (ps.rtau > ps.cd.tau) {
     ps.cd.tau = ps.rtau;
     ps.cd.tau_x = key_value(ps.rtau);
-    ps.cd.trimmed = true;
+    if (!ps.minp_floor) ps.cd.trimmed = true;
   }
 }
 
@@ -86,13 +93,13 @@ __device__ __forceinline__ void share_threshold(const SampleArgs& a, int64_t row
 // part's floor lies below the row's min-p cut, so the largest one serves all
 // parts of the row.
 __device__ __forceinline__ void raise_to_floor(PartState& ps) {
-  if (ps.floor > ps.cd.tau_x) {
-    const uint64_t fk = (uint64_t)ordkey(ps.floor) << 32;
+  const uint64_t fk = (uint64_t)ordkey(ps.floor) << 32;
+  if (ps.floor > -INFINITY && fk > ps.fkey) {
+    ps.fkey = fk;
+    ps.published = true;
     if (fk > ps.cd.tau) {
       ps.cd.tau = fk;
       ps.cd.tau_x = key_value(fk);
-      ps.cd.trimmed = true;
-      ps.published = true;
     }
   }
 }
@@ -460,6 +467,11 @@ __device__ __forceinline__ void part_end(const SampleArgs& a, int64_t row, int64
     if (lane == 0) a.best[row * a.max_parts + part] = wk;
   } else if (ps.mode == kCand) {
     if (ps.cd.cnt > ps.K) cand_compact<CAP>(wm->cand, wm->hist, ps.cd, ps.K);
+    // the part's final threshold bounds the row's K-th key (or its min-p
+    // cut) from below: the merge starts from the largest one
+    const uint64_t b = part_bound(ps);
+    if (lane == 0 && b) atomicMax(reinterpret_cast<unsigned long long*>(&a.row_tau[row]), b);
+    if (lane == 0) a.best[row * a.max_parts + part] = ps.cd.ctau;
     uint64_t* dst = a.cand + (row * a.max_parts + part) * (int64_t)KC;
     for (int i = lane; i < ps.cd.cnt; i += 32) dst[i] = wm->cand[i];
     if (lane == 0) a.cand_n[row * a.max_parts + part] = ps.cd.cnt | (ps.cd.trimmed ? (1 << 30) : 0);
@@ -527,18 +539,36 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
       continue;
     }
     const int K = (p.top_k > 0 && p.top_k < KC) ? p.top_k : KC;
-    // 1. each warp: parts wid, wid + 8, ... into its own top-K; a round takes
-    //    32 of the warp's parts at once (lane i: part wid + 8 (p0 + i)), their
-    //    keys flattened and loaded eight per lane in flight
-    {
+    const bool needx = needs_xstats(a, p, mode);
+    // 1. warp 0: the row log-sum-exp.  Warps 1..7 (fw = wid - 1): parts fw,
+    //    fw + 7, ... into their own top-K, from the row's shared threshold; a
+    //    round takes 32 of the warp's parts at once (lane i: part
+    //    fw + 7 (p0 + i)), their keys flattened and loaded eight per lane in
+    //    flight
+    if (wid == 0) {
+      if (needx) {
+        float mx;
+        const float c = warp_combine(a.statx + row * a.n_tiles, a.n_tiles, &mx);
+        if (lane == 0) mc->lse = c;
+      }
+      if (lane == 0) { mc->wcnt[0] = 0; mc->wtrim[0] = 0; }
+    } else {
+      const int fw = wid - 1;
       Cand cd;
       cand_reset(cd);
+      const bool minp = minp_floor_row(p);
+      const uint64_t rt = ld_cg(&a.row_tau[row]);
+      if (rt) {
+        cd.tau = rt;
+        cd.tau_x = key_value(rt);
+        cd.trimmed = !minp;
+      }
       bool trimmed = false;
-      const int mine_n = n_parts > wid ? (n_parts - wid + 7) / 8 : 0;
+      const int mine_n = n_parts > fw ? (n_parts - fw + 6) / 7 : 0;
       for (int p0 = 0; p0 < mine_n; p0 += 32) {
-        const int part = wid + 8 * (p0 + lane);
+        const int part = fw + 7 * (p0 + lane);
         const int raw = p0 + lane < mine_n ? ld_cg(&a.cand_n[row * a.max_parts + part]) : 0;
-        trimmed |= __any_sync(kFull, (raw >> 30) & 1) != 0;
+        trimmed |= __any_sync(kFull, part_trimmed(a, row, part, raw, minp, rt)) != 0;
         const int n = raw & 0x3fffffff;
         const int incl = warp_incl_scan(n);
         const int tot = __shfl_sync(kFull, incl, 31);
@@ -558,7 +588,7 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
             const int nq = __shfl_sync(kFull, n, qi);
             keys[u] = 0ull;
             if (f < tot) {
-              const uint64_t* src = a.cand + (row * a.max_parts + wid + 8 * (p0 + qi)) * (int64_t)KC;
+              const uint64_t* src = a.cand + (row * a.max_parts + fw + 7 * (p0 + qi)) * (int64_t)KC;
               keys[u] = ld_cg(&src[f - (iq - nq)]);
             }
           }
@@ -591,14 +621,8 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
     dropped |= tot > K;
     const int ncarry = block_topk_sorted(mc->u, tot, K, mc->carry, KC, mc->mhist, mc->scal);
     __syncthreads();
-    // 3. log-sum-exp (warp 0) beside the Gumbel scores (the other warps)
-    const bool needx = needs_xstats(a, p, mode);
-    if (wid == 0 && needx) {
-      float mx;
-      const float c = warp_combine(a.statx + row * a.n_tiles, a.n_tiles, &mx);
-      if (lane == 0) mc->lse = c;
-    }
-    for (int r = tid - 32; r >= 0 && r < ncarry; r += 256 - 32)
+    // 3. the Gumbel scores of the row's top-K
+    for (int r = tid; r < ncarry; r += 256)
       mc->score[r] = fadd(fmul(key_value(mc->carry[r]), p.inv_temperature), row_gumbel(a, row, key_index(mc->carry[r])));
     __syncthreads();
     // 4. filters and draw

@@ -70,9 +70,11 @@ __global__ void __launch_bounds__(256) k_shard_pack(const __grid_constant__ Samp
       const int K = (p.top_k > 0 && p.top_k < KC) ? p.top_k : KC;
       Cand cd;
       cand_reset(cd);
+      const bool minp = minp_floor_row(p);
+      const uint64_t rt = minp ? ld_cg(&a.row_tau[row]) : 0ull;
       for (int part = 0; part < n_parts; ++part) {
         const int raw = ld_cg(&a.cand_n[row * a.max_parts + part]);
-        trimmed |= (raw >> 30) & 1;
+        trimmed |= part_trimmed(a, row, part, raw, minp, rt);
         const int n = raw & 0x3fffffff;
         const uint64_t* src = a.cand + (row * a.max_parts + part) * (int64_t)KC;
         for (int i0 = 0; i0 < n; i0 += 32)

@@ -226,6 +226,14 @@ __device__ __forceinline__ int row_mode(const pm_row_params& p) {
   return kFullDraw;
 }
 
+// Rows filtered by min-p alone (top-k and top-p off, min_tokens_to_keep <= 1):
+// nothing below (any part's maximum) + log(min_p) - 1 can survive, so such a
+// floor is a candidate threshold that drops no survivor.  The shared row
+// threshold of these rows carries floors only.
+__device__ __forceinline__ bool minp_floor_row(const pm_row_params& p) {
+  return (p.flags & PM_F_MIN_P) && !(p.flags & PM_F_TOP_P) && p.top_k <= 0 && p.min_tokens_to_keep <= 1;
+}
+
 __device__ __forceinline__ bool needs_xstats(const SampleArgs& a, const pm_row_params& p, int mode) {
   return a.want_lse || (mode == kCand && (p.flags & (PM_F_TOP_P | PM_F_MIN_P)));
 }

@@ -16,6 +16,7 @@ struct Cand {
   uint64_t tau;   // smallest key kept by the last compaction (0: none yet)
   float tau_x;    // its value, for the cheap pre-test
   bool trimmed;   // a compaction dropped keys
+  uint64_t ctau;  // the last compaction's threshold (keys it dropped lie below)
 };
 
 __device__ __forceinline__ void cand_reset(Cand& c) {
@@ -23,6 +24,7 @@ __device__ __forceinline__ void cand_reset(Cand& c) {
   c.tau = 0;
   c.tau_x = -INFINITY;
   c.trimmed = false;
+  c.ctau = 0;
 }
 
 // Keep the K largest of buf[0..cnt) (cnt > K); returns the smallest kept key.
@@ -38,6 +40,7 @@ __device__ __forceinline__ void cand_compact(uint64_t* buf, unsigned* hist, Cand
   c.tau_x = key_value(c.tau);
   c.cnt = K;
   c.trimmed = true;
+  c.ctau = c.tau;
 }
 
 // Offer VW consecutive values per lane (tokens tok0 .. tok0+VW-1; lmax their
@@ -462,6 +465,16 @@ __device__ __noinline__ int warp_full_draw(const SampleArgs& a, const pm_row_par
   return tok;
 }
 
+// A part list's trimmed bit as a merge reads it.  On min-p floor rows a list
+// whose compactions cut only at or below the row's shared floor rt still
+// holds every survivor: its last compaction threshold (kept in the part's
+// best slot, unused by such rows) decides.
+__device__ __forceinline__ bool part_trimmed(const SampleArgs& a, int64_t row, int part, int raw, bool minp,
+                                             uint64_t rt) {
+  if (!((raw >> 30) & 1)) return false;
+  return !(minp && rt && ld_cg(&a.best[row * a.max_parts + part]) <= rt);
+}
+
 // Row merge by the warp that completed the row: gathers the parts' results
 // and draws the token.  Returns the token (-1 when flagged); *x_tok the
 // chosen token's processed logit, *lse the row log-sum-exp (NaN if unused).
@@ -491,6 +504,14 @@ __device__ __noinline__ int warp_row_merge(const SampleArgs& a, int64_t row, int
     const int K = (p.top_k > 0 && p.top_k < KC) ? p.top_k : KC;
     Cand cd;
     cand_reset(cd);
+    // the row's shared threshold: the largest bound the parts published
+    const bool minp = minp_floor_row(p);
+    const uint64_t rt = ld_cg(&a.row_tau[row]);
+    if (rt) {
+      cd.tau = rt;
+      cd.tau_x = key_value(rt);
+      cd.trimmed = !minp;
+    }
     // Parts in groups of 32: the counts in one round of loads (lane i: part
     // p0+i), then the group's keys in flattened order, eight independent
     // loads per lane per round; a key's part is found by a binary search
@@ -500,7 +521,7 @@ __device__ __noinline__ int warp_row_merge(const SampleArgs& a, int64_t row, int
       const int part = p0 + lane;
       const int raw = part < n_parts ? ld_cg(&a.cand_n[row * a.max_parts + part]) : 0;
       const int n = raw & 0x3fffffff;
-      trimmed_any |= __any_sync(kFull, (raw >> 30) & 1) != 0;
+      trimmed_any |= __any_sync(kFull, part_trimmed(a, row, part, raw, minp, rt)) != 0;
       const int incl = warp_incl_scan(n);
       const int tot = __shfl_sync(kFull, incl, 31);
       for (int f0 = 0; f0 < tot; f0 += 256) {
