@@ -34,6 +34,7 @@ struct PrepArgs {
   uint32_t* ovr_info; // [rows, cap]
   int32_t* ovr_off;   // [rows, n_tiles + 1]
   int32_t* status;    // [rows]
+  uint64_t* row_tau;  // [rows] zeroed here for the streaming pass (or null)
 };
 
 __device__ __forceinline__ int window_start(int H, int ctx) {
@@ -58,7 +59,11 @@ __global__ void __launch_bounds__(1024) k_prep_overrides(PrepArgs a) {
   int* tcur = tcount + 264;    // [264]
   const int tid = threadIdx.x, nth = blockDim.x;
   const int64_t r = blockIdx.x;
+  // the streaming pass may start its prologue (tile loads) now; it waits for
+  // this grid before it reads anything written here
+  asm volatile("griddepcontrol.launch_dependents;");
   if (r >= a.rows) return;
+  if (a.row_tau && tid == 0) a.row_tau[r] = 0;
   const pm_row_params p = a.params[a.params_per_row ? r : 0];
   const int64_t b = a.feed ? r / a.feed_group : r;
   const int fi = a.feed ? (int)(r % a.feed_group) : -1;

@@ -706,6 +706,9 @@ __global__ void __launch_bounds__(kThreadsS, 3) k_sample_stream(const __grid_con
     if (g0 + s < g1 && issue_tile<T, KC>(a, irow, itile, s, wm, pol)) armed |= 1u << s;
     if (++itile == a.n_tiles) { itile = 0; ++irow; }
   }
+  // the kernel before (the penalty prep, when it runs) has finished and its
+  // writes are visible past this point
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   PartState ps;
   part_begin(a, row, tile, KC, ps);
   int s = 0;
@@ -1018,6 +1021,7 @@ int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::Sample
     pa.ovr_info = reinterpret_cast<uint32_t*>(ws + L.ovr_info);
     pa.ovr_off = reinterpret_cast<int32_t*>(ws + L.ovr_off);
     pa.status = a.status;
+    pa.row_tau = a.row_tau;
     const size_t smem = sizeof(int) * (6 * (size_t)L.ovr_cap + 2 * 264);
     static std::once_flag once;
     std::call_once(once, [] {
@@ -1054,13 +1058,34 @@ int launch_stream(const pm::SampleArgs& a, bool cand_rows, cudaStream_t st, bool
   const int64_t grid = (a.n_warps + pm::kWarpsS - 1) / pm::kWarpsS;
   if (grid == 0) return PM_OK;
   cudaError_t e;
-  if (cand_rows) {  // the shared row thresholds start at zero ("nothing proven")
+  // the shared row thresholds start at zero ("nothing proven"); the penalty
+  // prep zeroes them when it runs
+  if (cand_rows && !a.prep_ran) {
     e = cudaMemsetAsync(a.row_tau, 0, sizeof(uint64_t) * a.rows, st);
     if (e != cudaSuccess) return cuda_fail(e);
   }
-  pm::k_sample_stream<T, KC><<<(unsigned)grid, pm::kThreadsS, smem, st>>>(a);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e);
+  {
+    // programmatic dependent launch: the tile prologue overlaps the tail of
+    // the kernel before (the penalty prep); the kernel waits for it before
+    // reading its outputs
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(pm::kThreadsS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, pm::k_sample_stream<T, KC>, a);
+    if (e != cudaSuccess) {
+      cudaGetLastError();  // no programmatic launch here: plain stream order
+      pm::k_sample_stream<T, KC><<<(unsigned)grid, pm::kThreadsS, smem, st>>>(a);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(e);
+    }
+  }
   if (!merge) return PM_OK;
   // the row merges, chained by programmatic dependent launch: one CTA per
   // row when rows are few (every row then has many parts), one warp per row
