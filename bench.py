@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--c5-rows", type=int, default=1024,
+                    help="rows of the C5 workload (smaller only for profiling captures)")
     ap.add_argument("--workload", default="c3", choices=["c3", "c5", "c1", "c2", "c2b", "c4a", "c4b"],
                     help="c3 (default): the headline metric's config; c5: vocabulary-sharded sampling over the ranks")
     return ap.parse_args()
@@ -376,7 +378,7 @@ def run_c5(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     from paged_moe_b200 import shard as S
     from paged_moe_b200.params import SamplerSettings
-    B, V = 1024, 262144
+    B, V = args.c5_rows, 262144
     spec = S.ShardSpec.of(rank, world, V)
     w = spec.hi - spec.lo
     s = SamplerSettings(temp=0.8, top_k=64, top_p=0.9)
@@ -428,7 +430,7 @@ def run_c5(args):
         "metric": "sampled rows/s, vocabulary-sharded C5", "value": B / (ms_step / 1000.0), "unit": "rows/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"C5: 1,024 rows, V=262,144 fp32 in {world} slices of {w} ids, temp 0.8, top_k 64, "
+        "config": {"workload": f"C5: {B:,} rows, V=262,144 fp32 in {world} slices of {w} ids, temp 0.8, top_k 64, "
                                "top_p 0.9; summarize + all-gather + merge per step",
                    "l2": "two alternating input batches larger than L2 per rank" if B * w * 4 > 126e6 else
                          "two alternating input batches"},

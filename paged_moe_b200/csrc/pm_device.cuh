@@ -53,10 +53,10 @@ __device__ __forceinline__ float det_expf(float d) {
 }
 
 // floor(e * 2^52) of a positive normal fp32 e below 2^7, from its bits:
-// e = mant * 2^(E - 150), so e * 2^52 = mant * 2^(E - 98), exactly.
+// adding 52 to the exponent field gives e * 2^52 exactly (a float below 2^59),
+// and the truncating conversion to a 64-bit integer is then exact.
 __device__ __forceinline__ uint64_t q52_from_bits(uint32_t be) {
-  const uint64_t mant = (uint64_t)((be & 0x7FFFFFu) | 0x800000u);
-  return (mant << 32) >> (130u - (be >> 23));
+  return __float2ull_rz(__uint_as_float(be + (52u << 23)));
 }
 
 // floor(e^d * 2^52) with e^d = det_expf(d); 0 for d < -38, -inf or NaN.
