@@ -470,8 +470,10 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
         __syncthreads();
         const int ns = mm->nsel;
         if (ns <= kSel) {
-          for (int i = tid; i < ncarry; i += kMThreads) mm->sel[ns + i] = mm->carry[i];
-          __syncthreads();
+          if (ncarry) {  // CTA-uniform: nothing carried into the first window
+            for (int i = tid; i < ncarry; i += kMThreads) mm->sel[ns + i] = mm->carry[i];
+            __syncthreads();
+          }
           const int total = ns + ncarry;
           dropped |= total > K;
           if (total <= 512) {
@@ -547,7 +549,7 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
         __syncthreads();
         tau = ncarry == K ? mm->carry[K - 1] : 0ull;
       }
-      __syncthreads();
+      if (mode != kCand) __syncthreads();  // (candidate rows have just passed one)
       t0 = t1;
     }
     // 3. the draw.  Log-sum-exp by the whole CTA: thread t weighs tile t
@@ -595,14 +597,8 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
           x_tok = key_value(best);
         }
       } else if (mode == kCand) {
-        tok = warp_filter_draw(a, p, row, mm->carry, ncarry, !dropped, c, &ns, mm->score);
-        if (tok >= 0) {
-          float fx = -INFINITY;
-          for (int r = lane; r < ncarry; r += 32)
-            if ((int)key_index(mm->carry[r]) == tok) fx = key_value(mm->carry[r]);
-          x_tok = warp_max(fx);
-          if (a.surv_ids && lane == 0) write_survivors(a, p, row, mm->carry, ns);
-        }
+        tok = warp_filter_draw(a, p, row, mm->carry, ncarry, !dropped, c, &ns, mm->score, &x_tok);
+        if (tok >= 0 && a.surv_ids && lane == 0) write_survivors(a, p, row, mm->carry, ns);
       } else {
         tok = warp_full_draw<T>(a, p, row, &x_tok);  // reads the y statistics this CTA wrote
       }

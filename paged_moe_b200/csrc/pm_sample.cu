@@ -629,15 +629,9 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
     if (wid == 0) {
       const float c = needx ? mc->lse : __int_as_float(0x7fc00000);
       int ns = 0;
-      const int tok = warp_filter_draw(a, p, row, mc->carry, ncarry, !dropped, c, &ns, mc->score);
-      float x_tok = -INFINITY;
-      if (tok >= 0) {
-        float fx = -INFINITY;
-        for (int r = lane; r < ncarry; r += 32)
-          if ((int)key_index(mc->carry[r]) == tok) fx = key_value(mc->carry[r]);
-        x_tok = warp_max(fx);
-        if (a.surv_ids && lane == 0) write_survivors(a, p, row, mc->carry, ns);
-      }
+      float x_tok;
+      const int tok = warp_filter_draw(a, p, row, mc->carry, ncarry, !dropped, c, &ns, mc->score, &x_tok);
+      if (tok >= 0 && a.surv_ids && lane == 0) write_survivors(a, p, row, mc->carry, ns);
       if (lane == 0) write_row(a, row, mode, tok, x_tok, c, ns);
     }
     __syncthreads();

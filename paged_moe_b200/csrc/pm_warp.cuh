@@ -242,18 +242,24 @@ __device__ __forceinline__ uint64_t row_u53(const SampleArgs& a, int64_t row, in
 //   draw:  argmax over survivors of fl32(fl32(x * inv_temp) + g), ties to the
 //          lowest id.
 // Returns the token, or -1 when the survivors reach past the candidates (the
-// row is then flagged; only possible when top_k is off).  *n_out = survivors.
+// row is then flagged; only possible when top_k is off).  *n_out = survivors;
+// *x_out (when given) = the token's value, S's value at its rank.
 __device__ int warp_filter_draw(const SampleArgs& a, const pm_row_params& p, int64_t row, const uint64_t* S,
-                                int m, bool complete, float c, int* n_out, const float* scores = nullptr) {
+                                int m, bool complete, float c, int* n_out, const float* scores = nullptr,
+                                float* x_out = nullptr) {
   const int lane = threadIdx.x & 31;
   *n_out = 0;
+  if (x_out) *x_out = -INFINITY;
   if (m == 0) return 0;
   const bool topk = p.top_k > 0;
   int cnt = (topk && p.top_k < m) ? p.top_k : m;
   bool determined = topk || complete;
   if (p.flags & PM_F_TOP_P) {
-    uint64_t T = 0;
-    for (int r = lane; r < cnt; r += 32) T += q52(fsub(key_value(S[r]), c));
+    // q52 of the first 64 ranks once, kept for the cut search below
+    const uint64_t qa = lane < cnt ? q52(fsub(key_value(S[lane]), c)) : 0ull;
+    const uint64_t qb = lane + 32 < cnt ? q52(fsub(key_value(S[lane + 32]), c)) : 0ull;
+    uint64_t T = qa + qb;
+    for (int r = lane + 64; r < cnt; r += 32) T += q52(fsub(key_value(S[r]), c));
     T = warp_sum_u64(T);
     if (!topk) T = 1ull << 52;
     const uint64_t qthr = __float2ull_rz(fmul(p.top_p_comp, 0x1p52f));
@@ -262,7 +268,7 @@ __device__ int warp_filter_draw(const SampleArgs& a, const pm_row_params& p, int
     bool found = false;
     for (int base = 0; base < cnt && !found; base += 32) {
       const int r = base + lane;
-      const uint64_t q = r < cnt ? q52(fsub(key_value(S[r]), c)) : 0ull;
+      const uint64_t q = base == 0 ? qa : base == 32 ? qb : r < cnt ? q52(fsub(key_value(S[r]), c)) : 0ull;
       const uint64_t incl = warp_incl_scan_u64(q);
       const uint64_t A = carry + incl - q;
       const bool ok = r < cnt && A < T && (T - A) > qthr;
@@ -288,19 +294,21 @@ __device__ int warp_filter_draw(const SampleArgs& a, const pm_row_params& p, int
   }
   if (!determined) return -1;
   float bs = -INFINITY;
-  int bid = -1;
+  int bid = -1, brank = -1;
   for (int r = lane; r < cnt; r += 32) {
     const uint32_t id = key_index(S[r]);
     const float sc = scores ? scores[r] : fadd(fmul(key_value(S[r]), p.inv_temperature), row_gumbel(a, row, id));
-    if (bid < 0 || sc > bs || (sc == bs && (int)id < bid)) { bs = sc; bid = (int)id; }
+    if (bid < 0 || sc > bs || (sc == bs && (int)id < bid)) { bs = sc; bid = (int)id; brank = r; }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float os = __shfl_xor_sync(kFull, bs, o);
     const int oid = __shfl_xor_sync(kFull, bid, o);
-    if (oid >= 0 && (bid < 0 || os > bs || (os == bs && oid < bid))) { bs = os; bid = oid; }
+    const int ork = __shfl_xor_sync(kFull, brank, o);
+    if (oid >= 0 && (bid < 0 || os > bs || (os == bs && oid < bid))) { bs = os; bid = oid; brank = ork; }
   }
   *n_out = cnt;
+  if (x_out && brank >= 0) *x_out = key_value(S[brank]);
   return bid;
 }
 
