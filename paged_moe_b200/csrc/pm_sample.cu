@@ -1214,7 +1214,8 @@ struct VLayout {
   Layout L;
   int k = 0, scap = 0;
   int64_t B = 0, D = 0;
-  size_t rtok = 0, sids = 0, sprobs = 0, ns = 0, pending = 0, dstat = 0, dlse = 0, ylse = 0, rsum = 0, total = 0;
+  size_t rtok = 0, sids = 0, sprobs = 0, ns = 0, pending = 0, dstat = 0, dlse = 0, ylse = 0, rsum = 0, probs = 0,
+         total = 0;
 };
 
 int plan_verify(const pm_rows* r, const pm_verify_args* v, VLayout* V) {
@@ -1241,6 +1242,7 @@ int plan_verify(const pm_rows* r, const pm_verify_args* v, VLayout* V) {
   V->dlse = take(sizeof(float) * V->D);
   V->ylse = take(sizeof(float) * V->B);
   V->rsum = take(res ? sizeof(uint64_t) * V->B * V->L.n_tiles : 0);
+  V->probs = take(sizeof(pm::AccProb) * V->D);
   V->total = align_up(o, 256);
   return PM_OK;
 }
@@ -1453,6 +1455,14 @@ int pm_verify(const pm_rows* rows, const pm_noise* noise, const pm_verify_args* 
   vk.pending = reinterpret_cast<int32_t*>(ws + V.pending);
   vk.ylse = reinterpret_cast<float*>(ws + V.ylse);
   vk.rsum = reinterpret_cast<uint64_t*>(ws + V.rsum);
+  vk.probs = reinterpret_cast<pm::AccProb*>(ws + V.probs);
+  if (res && V.D > 0) {
+    int64_t g = (V.D + 7) / 8;
+    if (g > (int64_t)num_sms() * 8) g = (int64_t)num_sms() * 8;
+    pm::k_accept_probs<<<(unsigned)g, 256, 0, st>>>(a, rows->dtype, vk);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
   rc = V.L.KC == 64 ? launch_accept<64>(a, rows->dtype, vk, V.B, st) : launch_accept<256>(a, rows->dtype, vk, V.B, st);
   if (rc) return rc;
   if (res && V.k > 0 && (rows->flags_any & PM_F_FULL)) {

@@ -19,6 +19,16 @@
 
 namespace pm {
 
+// What the acceptance test of one draft position needs, computed for every
+// position at once (k_accept_probs) before the sequential walk.
+struct AccProb {
+  float pd;       // target probability of the draft token
+  float qd;       // draft probability of the draft token
+  float cy;       // whole-vocabulary rows: the row's log-sum-exp of y = x / temp
+  int32_t wide;   // filtered rows whose survivors outrun the candidate lists
+};
+static_assert(sizeof(AccProb) == 16, "read as one 16-byte load");
+
 struct VerifyK {
   int32_t mode;
   const int32_t* drafts;   // [B, k]
@@ -40,6 +50,7 @@ struct VerifyK {
   int32_t* pending;        // [B] row awaiting a whole-vocabulary residual draw, -1 if none
   float* ylse;             // [B] that row's log-sum-exp of y = x / temp
   uint64_t* rsum;          // [B, n_tiles] residual mass of each tile of that row
+  AccProb* probs;          // [B, k] residual mode: every position's acceptance inputs
 };
 
 __device__ __forceinline__ float draft_value(const VerifyK& v, int64_t drow, int64_t tok) {
@@ -107,6 +118,62 @@ __device__ int survivor_residual(const SampleArgs& a, const VerifyK& v, int64_t 
   return -1;
 }
 
+__device__ __forceinline__ AccProb ld_cg_accprob(const AccProb* p) {
+  const float4 f = __ldcg(reinterpret_cast<const float4*>(p));
+  AccProb r;
+  r.pd = f.x;
+  r.qd = f.y;
+  r.cy = f.z;
+  r.wide = __float_as_int(f.w);
+  return r;
+}
+
+// Residual mode, before the acceptance walk: one warp per draft position
+// (request b, position i) computes p(d_i), q(d_i) and, for whole-vocabulary
+// rows, the row's log-sum-exp of y, with the same arithmetic the walk used to
+// apply position by position.
+__global__ void __launch_bounds__(256) k_accept_probs(const __grid_constant__ SampleArgs a, int dtype,
+                                                      const __grid_constant__ VerifyK v) {
+  const int lane = threadIdx.x & 31;
+  const int K1 = v.k + 1;
+  const int64_t D = (a.rows / K1) * v.k;
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < D;
+       w += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    const int64_t b = w / v.k;
+    const int i = (int)(w - b * v.k);
+    const int64_t row = b * K1 + i;
+    const pm_row_params p = row_params(a, row);
+    const int mode = row_mode(p);
+    const int d = v.drafts[w];
+    AccProb r;
+    r.qd = draft_prob(v, w, d, ld_cg(&v.dlse[w]));
+    r.cy = 0.0f;
+    r.wide = 0;
+    r.pd = 0.0f;
+    if (mode == kGreedy) {
+      r.pd = ld_cg(&v.rtok[row]) == d ? 1.0f : 0.0f;
+    } else if (mode == kCand) {
+      const int n = ld_cg(&v.ns[row]);
+      if (n > v.scap) {
+        r.wide = 1;
+      } else {
+        float f = 0.0f;
+        for (int q = lane; q < n; q += 32)
+          if (ld_cg(&v.sids[row * v.scap + q]) == d) f = ld_cg(&v.sprobs[row * v.scap + q]);
+        r.pd = warp_max(f);
+      }
+    } else {
+      float m;
+      r.cy = warp_combine(a.staty + row * a.n_tiles, a.n_tiles, &m);
+      const float x = processed_value(a, dtype, p, row, d);
+      const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
+      r.pd = det_expf(fsub(y, r.cy));
+    }
+    if (lane == 0) v.probs[w] = r;
+    __syncwarp();
+  }
+}
+
 // Acceptance: one warp per request.
 template <int KC>
 __global__ void __launch_bounds__(256) k_verify_accept(const __grid_constant__ SampleArgs a, int dtype,
@@ -149,31 +216,14 @@ __global__ void __launch_bounds__(256) k_verify_accept(const __grid_constant__ S
       const int64_t drow = b * v.k + i;
       const pm_row_params p = row_params(a, row);
       const int mode = row_mode(p);
-      const int d = v.drafts[b * v.k + i];
       const float cd = ld_cg(&v.dlse[drow]);
-      const float q_d = draft_prob(v, drow, d, cd);
-      float p_d;
-      float cy = 0.0f;
-      if (mode == kGreedy) {
-        p_d = ld_cg(&v.rtok[row]) == d ? 1.0f : 0.0f;
-      } else if (mode == kCand) {
-        const int n = ld_cg(&v.ns[row]);
-        if (n > v.scap) {  // survivors beyond the candidate lists: this request cannot be judged exactly
-          wide = true;
-          break;
-        }
-        float f = 0.0f;
-        for (int r = lane; r < n; r += 32)
-          if (ld_cg(&v.sids[row * v.scap + r]) == d) f = ld_cg(&v.sprobs[row * v.scap + r]);
-        p_d = warp_max(f);
-      } else {
-        float m;
-        cy = warp_combine(a.staty + row * a.n_tiles, a.n_tiles, &m);
-        const float x = processed_value(a, dtype, p, row, d);
-        const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
-        p_d = det_expf(fsub(y, cy));
+      const AccProb pr = ld_cg_accprob(&v.probs[drow]);
+      if (pr.wide) {  // survivors beyond the candidate lists: this request cannot be judged exactly
+        wide = true;
+        break;
       }
-      if (dmul(accept_uniform(a, v, b, i, row), (double)q_d) < (double)p_d) continue;
+      const float cy = pr.cy;
+      if (dmul(accept_uniform(a, v, b, i, row), (double)pr.qd) < (double)pr.pd) continue;
       // first rejection at row i: a draw from max(p - q, 0)
       if (mode == kGreedy) {
         final_tok = ld_cg(&v.rtok[row]);  // the only token with a positive residual, or the row's own draw
