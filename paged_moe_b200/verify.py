@@ -69,11 +69,16 @@ def verify(target_logits: torch.Tensor, drafts: torch.Tensor, y: torch.Tensor, s
     keep = _Keep()
     drafts = keep(drafts.to(device=dev, dtype=torch.int32).contiguous())
     y = torch.as_tensor(y).reshape(B).to(device=dev, dtype=torch.int32)
-    feed = keep(torch.cat([y[:, None], drafts], dim=1).contiguous())
+    procs = _per_row(processors, B, K1)
+    # the feed (y, then the drafts) extends the history the penalties read;
+    # without a penalty nothing reads it
+    plist = procs if isinstance(procs, list) else [procs]
+    pens = any(p is not None and p.penalties_on for p in plist)
+    feed = keep(torch.cat([y[:, None], drafts], dim=1).contiguous()) if pens else None
     if mask is not None and mask.dim() == 3:
         mask = mask.reshape(B * K1, -1)
-    r = build_rows(x, _per_row(sampler, B, K1), _per_row(processors, B, K1), history, history_len, mask, keep,
-                   feed=feed, feed_group=K1)
+    r = build_rows(x, _per_row(sampler, B, K1), procs, history, history_len, mask, keep,
+                   feed=feed, feed_group=K1 if pens else 0)
     nz = _noise(B * K1, V, seed, offset, row_base, gumbel, uniform, keep, dev)
     va = L.VerifyArgs()
     va.mode = _MODES[mode]
