@@ -5,10 +5,10 @@
 // (a grammar state, a forced token).  Every processed value of a disallowed
 // token is -inf and contributes nothing to the row's log-sum-exp, candidates
 // or draw, so this pass reads the row's mask words first and then fetches
-// only the logits of allowed tokens: asynchronous 4-byte copies
-// (cp.async, L2 evict-first) into a shared-memory window, compacted in
-// ascending token order.  The HBM traffic is the mask plus the 32-byte
-// sectors that hold an allowed token, instead of the whole row.
+// only the logits of allowed tokens: 4-byte loads cached in L2 only, many in
+// flight per thread, into a shared-memory window compacted in ascending
+// token order.  The HBM traffic is the mask plus the 32-byte sectors that
+// hold an allowed token, instead of the whole row.
 //
 // Per row (8 warps, one CTA):
 //   1. mask words -> shared memory (cut at the vocabulary), allowed count per
@@ -101,15 +101,6 @@ __device__ __forceinline__ void smem_add_u64(uint64_t* dst, uint64_t v) {
   if (hi) atomicAdd(&w[1], hi);
 }
 
-__device__ __forceinline__ void cp_async4(void* dst, const void* src, uint64_t policy) {
-  asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
-               "l"(policy)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
-
 // The processed logit of one token of a row (bias, penalties, mask): the
 // single-token form of process_tile, for the rare paths.
 __device__ float processed_value(const SampleArgs& a, int dtype, const pm_row_params& p, int64_t row, int tok) {
@@ -181,7 +172,6 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
   const int nt = a.n_tiles;
   const int nw = (int)((a.vocab + 31) >> 5);
   const int KW = (nt * 32 + kMThreads - 1) / kMThreads;  // mask-word rounds: word tid + 256 k is in tile 8 k + wid
-  const uint64_t pol = policy_evict_first();
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
     const pm_row_params p = row_params(a, row);
     const int mode = row_mode(p);
@@ -259,7 +249,7 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
       }
       const int t1 = lo;
       const int n = mm->toff[t1] - base;
-      // gather: lane per mask word, ascending token order inside the window
+      // the window's token ids in ascending order: lane per mask word
       for (int k = 0; k < KW; ++k) {
         const int tile = k * kMWarps + wid;
         if (tile < t0 || tile >= t1) continue;  // warp-uniform
@@ -268,20 +258,33 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
         int pos = mm->toff[tile] - base + mm->wpre[w];
         const int id0 = w * 32;
         while (word) {
-          const int id = id0 + __ffs(word) - 1;
+          mm->ids[pos++] = (uint32_t)(id0 + __ffs(word) - 1);
           word &= word - 1;
-          cp_async4(&mm->val[pos], rowp + (sizeof(T) == 4 ? id : (id & ~1)), pol);
-          mm->ids[pos] = (uint32_t)id;
-          ++pos;
         }
       }
-      cp_async_wait_all();
       __syncthreads();
-      if constexpr (sizeof(T) == 2) {
-        for (int i = tid; i < n; i += kMThreads)
-          mm->val[i] = __float_as_uint(staged_value<T>(mm->val[i], (int)mm->ids[i]));
-        __syncthreads();
+      // their logits: 4-byte loads cached in L2 only (one 32-byte sector
+      // each; an L1-allocating load would fill the whole 128-byte line), all
+      // kRun of a thread in flight before the shared-memory stores.  bf16
+      // rows load the 32-bit word holding the value and widen it here.
+      {
+        uint32_t v[kRun];
+#pragma unroll
+        for (int r = 0; r < kRun; ++r) {
+          const int i = tid + r * kMThreads;
+          v[r] = 0u;
+          if (i < n) {
+            const uint32_t id = mm->ids[i];
+            v[r] = __ldcg(reinterpret_cast<const unsigned int*>(rowp + (sizeof(T) == 4 ? id : (id & ~1u))));
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < kRun; ++r) {
+          const int i = tid + r * kMThreads;
+          if (i < n) mm->val[i] = sizeof(T) == 4 ? v[r] : __float_as_uint(staged_value<T>(v[r], (int)mm->ids[i]));
+        }
       }
+      __syncthreads();
       // processors on the window's overridden ids (bias first, then penalties)
       if (a.bias_off) {
         for (int i = a.bias_off[t0] + tid; i < a.bias_off[t1]; i += kMThreads) {
