@@ -249,17 +249,31 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
       }
       const int t1 = lo;
       const int n = mm->toff[t1] - base;
-      // the window's token ids in ascending order: lane per mask word
-      for (int k = 0; k < KW; ++k) {
-        const int tile = k * kMWarps + wid;
-        if (tile < t0 || tile >= t1) continue;  // warp-uniform
-        const int w = tid + k * kMThreads;
-        uint32_t word = mm->mw[w];
-        int pos = mm->toff[tile] - base + mm->wpre[w];
-        const int id0 = w * 32;
-        while (word) {
-          mm->ids[pos++] = (uint32_t)(id0 + __ffs(word) - 1);
-          word &= word - 1;
+      // the window's token ids in ascending order: lane per mask word, the
+      // words and offsets of eight rounds loaded before their bit loops
+#pragma unroll
+      for (int k0 = 0; k0 < kMaxPer * 4; k0 += 8) {
+        if (k0 >= KW) break;  // CTA-uniform
+        uint32_t wv[8];
+        int pv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int k = k0 + u;
+          const int tile = k * kMWarps + wid;
+          const bool in = k < KW && tile >= t0 && tile < t1;
+          const int w = tid + k * kMThreads;
+          wv[u] = in ? mm->mw[w] : 0u;
+          pv[u] = in ? mm->toff[tile] - base + mm->wpre[w] : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          uint32_t word = wv[u];
+          int pos = pv[u];
+          const int id0 = (tid + (k0 + u) * kMThreads) * 32;
+          while (word) {
+            mm->ids[pos++] = (uint32_t)(id0 + __ffs(word) - 1);
+            word &= word - 1;
+          }
         }
       }
       __syncthreads();
