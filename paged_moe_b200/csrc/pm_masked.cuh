@@ -46,6 +46,8 @@ struct MaskedMem {
   uint32_t tmy[kMaxTiles];    // tile maxima of y = x * inv_temperature
   uint64_t tsx[kMaxTiles];    // tile sums of q52(x - m_t)
   uint64_t tsy[kMaxTiles];
+  uint32_t tsx3[kMaxTiles][3];  // the sums while they accumulate: 21-bit digits of each addend
+  uint32_t tsy3[kMaxTiles][3];
   int toff[kMaxTiles + 1];    // allowed tokens before each tile
   unsigned hist[256];
   int scal[8];
@@ -90,15 +92,18 @@ __device__ __forceinline__ bool seg_head(int seg) {
   return (threadIdx.x & 31) == 0 || prev != seg;
 }
 
-// dst += v for a 64-bit shared-memory counter, as two native 32-bit atomic
-// adds: the carry out of the low word is read from the value it held.  Exact
-// while the high word does not overflow.
-__device__ __forceinline__ void smem_add_u64(uint64_t* dst, uint64_t v) {
-  uint32_t* w = reinterpret_cast<uint32_t*>(dst);
-  const uint32_t lo = (uint32_t)v;
-  const uint32_t old = atomicAdd(&w[0], lo);
-  const uint32_t hi = (uint32_t)(v >> 32) + (old + lo < old ? 1u : 0u);
-  if (hi) atomicAdd(&w[1], hi);
+// A 64-bit sum accumulated in shared memory as three 32-bit counters, one
+// per 21-bit digit of each addend (v < 2^63): three native atomic adds that
+// return nothing, so no thread waits on them.  Exact while each counter
+// stays below 2^32: fewer than 2^11 addends, as a tile has at most 1024
+// values and each thread adds a tile's run once.
+__device__ __forceinline__ void smem_add3(uint32_t* c, uint64_t v) {
+  atomicAdd(&c[0], (uint32_t)(v & 0x1FFFFFu));
+  atomicAdd(&c[1], (uint32_t)((v >> 21) & 0x1FFFFFu));
+  atomicAdd(&c[2], (uint32_t)(v >> 42));
+}
+__device__ __forceinline__ uint64_t sum3(const uint32_t* c) {
+  return ((uint64_t)c[2] << 42) + ((uint64_t)c[1] << 21) + (uint64_t)c[0];
 }
 
 // The processed logit of one token of a row (bias, penalties, mask): the
@@ -212,6 +217,11 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
     mm->tmy[tid] = 0;
     mm->tsx[tid] = 0;
     mm->tsy[tid] = 0;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      mm->tsx3[tid][j] = 0;
+      mm->tsy3[tid][j] = 0;
+    }
     __syncthreads();
     if (wid == 0) {
       int c[kMaxPer];
@@ -391,8 +401,8 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
             if (r + h < len) {
               const int seg = (int)(h ? s1 : s0);
               if (seg != cur) {
-                if (sx) smem_add_u64(&mm->tsx[cur], sx);
-                if (sy) smem_add_u64(&mm->tsy[cur], sy);
+                if (sx) smem_add3(mm->tsx3[cur], sx);
+                if (sy) smem_add3(mm->tsy3[cur], sy);
                 cur = seg;
                 sx = sy = 0;
               }
@@ -402,8 +412,8 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
           }
         }
         if (len > 0) {
-          if (sx) smem_add_u64(&mm->tsx[cur], sx);
-          if (sy) smem_add_u64(&mm->tsy[cur], sy);
+          if (sx) smem_add3(mm->tsx3[cur], sx);
+          if (sy) smem_add3(mm->tsy3[cur], sy);
         }
         __syncthreads();
         for (int t = t0 + tid; t < t1; t += kMThreads) {
@@ -411,12 +421,14 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
           st.pad = 0;
           if (needx) {
             st.m = mm->tmx[t] ? ord_value(mm->tmx[t]) : -INFINITY;
-            st.s = mm->tsx[t];
+            st.s = sum3(mm->tsx3[t]);
+            mm->tsx[t] = st.s;
             a.statx[row * nt + t] = st;
           }
           if (needy) {
             st.m = mm->tmy[t] ? ord_value(mm->tmy[t]) : -INFINITY;
-            st.s = mm->tsy[t];
+            st.s = sum3(mm->tsy3[t]);
+            mm->tsy[t] = st.s;
             a.staty[row * nt + t] = st;
           }
         }
