@@ -63,8 +63,9 @@ __device__ __forceinline__ bool cand_offer_vec(const float (&x)[VW], float lmax,
   }
   c.cnt = base;
   __syncwarp();
-  // the first compaction comes early (K + 256 keys) to set a useful threshold
-  if (c.cnt > (c.trimmed ? CAP - 32 * VW : min(CAP - 32 * VW, K + 256))) {
+  // compactions come every 128 keys past K: a part's threshold then tracks
+  // its running K-th key closely enough that few later values pass it
+  if (c.cnt > min(CAP - 32 * VW, K + 128)) {
     cand_compact<CAP>(buf, hist, c, K);
     return true;
   }
