@@ -82,27 +82,23 @@ __device__ uint64_t warp_select_topk(uint64_t* buf, int cnt, int K, unsigned* hi
     if (in_bin == need || shift == 0) break;
     hi = shift;
   }
-  // keep keys >= prefix (low bits of prefix below `shift` are zero)
-  uint64_t mine[MAXPER];
-#pragma unroll
-  for (int r = 0; r < MAXPER; ++r) {
-    const int i = lane + 32 * r;
-    mine[r] = (i < cnt) ? buf[i] : 0ull;
-  }
-  __syncwarp();
+  // keep keys >= prefix (low bits of prefix below `shift` are zero), in
+  // place: a round's keys are read before any of its writes, and the writes
+  // land below the next round's keys
   uint64_t kept_min = ~0ull;
   int base = 0;
-#pragma unroll
-  for (int r = 0; r < MAXPER; ++r) {
-    const bool keep = (lane + 32 * r < cnt) && mine[r] >= prefix;
+  for (int r0 = 0; r0 < cnt; r0 += 32) {
+    const int i = r0 + lane;
+    const uint64_t k = i < cnt ? buf[i] : 0ull;
+    const bool keep = i < cnt && k >= prefix;
     const unsigned bal = __ballot_sync(kFull, keep);
     if (keep) {
-      buf[base + __popc(bal & ((1u << lane) - 1u))] = mine[r];
-      kept_min = mine[r] < kept_min ? mine[r] : kept_min;
+      buf[base + __popc(bal & ((1u << lane) - 1u))] = k;
+      kept_min = k < kept_min ? k : kept_min;
     }
     base += __popc(bal);
+    __syncwarp();
   }
-  __syncwarp();
   return warp_min_u64(kept_min);
 }
 
