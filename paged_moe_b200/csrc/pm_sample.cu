@@ -619,7 +619,21 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
       if (tid < mc->wcnt[w]) mc->u[start[w] + tid] = mine[w];
     __syncthreads();
     dropped |= tot > K;
-    const int ncarry = block_topk_sorted(mc->u, tot, K, mc->carry, KC, mc->mhist, mc->scal);
+    int ncarry;
+    if (tot <= 512) {
+      // few keys: rank each by counting the larger ones (unique keys), the K
+      // largest land sorted in the carry
+      for (int i = tid; i < tot; i += 256) {
+        const uint64_t k = mc->u[i];
+        int rank = 0;
+#pragma unroll 8
+        for (int j = 0; j < tot; ++j) rank += mc->u[j] > k;
+        if (rank < K) mc->carry[rank] = k;
+      }
+      ncarry = tot < K ? tot : K;
+    } else {
+      ncarry = block_topk_sorted(mc->u, tot, K, mc->carry, KC, mc->mhist, mc->scal);
+    }
     __syncthreads();
     // 3. the Gumbel scores of the row's top-K
     for (int r = tid; r < ncarry; r += 256)
