@@ -359,32 +359,36 @@ __device__ __forceinline__ void scan_tile_mode(const SampleArgs& a, int64_t row,
       raise_to_floor(ps);
     }
   }
-  if (MODE == kCand && dense && ps.cd.tau == 0 && ps.K <= 64) {
-    // the part's first offers: the K-th largest of the tile's 64 half-lane
-    // maxima (16 values each) bounds the part's K-th largest value from
-    // below, and so does its upper 16 key bits padded with zeros; the offers
-    // start there instead of at nothing.  Warp search, two bits a step.
+  if (MODE == kCand && dense && ps.cd.tau == 0 && ps.K <= 128) {
+    // the part's first offers: the K-th largest of the tile's 128
+    // quarter-lane maxima (8 values each) bounds the part's K-th largest
+    // value from below, and so does its upper 16 key bits padded with zeros;
+    // the offers start there instead of at nothing.  Warp search, two bits a
+    // step.
     constexpr int VW = Vec<S>::VW;
-    float h0 = -INFINITY, h1 = -INFINITY;
+    constexpr int SPQ = 8 / VW;  // steps per quarter (fp32: 2, bf16: 1)
+    float h[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
     for (int j = 0; j < 32 / VW; ++j) {
       float x[VW];
       read_step<S>(buf, j, lane, x);
 #pragma unroll
-      for (int c = 0; c < VW; ++c) {
-        if (j < 16 / VW) h0 = fmaxf(h0, x[c]);
-        else h1 = fmaxf(h1, x[c]);
-      }
+      for (int c = 0; c < VW; ++c) h[j / SPQ] = fmaxf(h[j / SPQ], x[c]);
     }
-    const uint32_t k0 = h0 > -INFINITY ? ordkey(h0) >> 16 : 0u;
-    const uint32_t k1 = h1 > -INFINITY ? ordkey(h1) >> 16 : 0u;
+    uint32_t kq[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) kq[q] = h[q] > -INFINITY ? ordkey(h[q]) >> 16 : 0u;
     uint32_t T = 0;
 #pragma unroll
     for (int b = 14; b >= 0; b -= 2) {
       const uint32_t c1 = T | (1u << b), c2 = T | (2u << b), c3 = T | (3u << b);
-      const unsigned n1 = (k0 >= c1 ? 1u : 0u) + (k1 >= c1 ? 1u : 0u);
-      const unsigned n2 = (k0 >= c2 ? 1u : 0u) + (k1 >= c2 ? 1u : 0u);
-      const unsigned n3 = (k0 >= c3 ? 1u : 0u) + (k1 >= c3 ? 1u : 0u);
+      unsigned n1 = 0, n2 = 0, n3 = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        n1 += kq[q] >= c1 ? 1u : 0u;
+        n2 += kq[q] >= c2 ? 1u : 0u;
+        n3 += kq[q] >= c3 ? 1u : 0u;
+      }
       const uint32_t d = ((int)__reduce_add_sync(kFull, n1) >= ps.K ? 1u : 0u) +
                          ((int)__reduce_add_sync(kFull, n2) >= ps.K ? 1u : 0u) +
                          ((int)__reduce_add_sync(kFull, n3) >= ps.K ? 1u : 0u);
