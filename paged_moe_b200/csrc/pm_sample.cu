@@ -684,12 +684,13 @@ __global__ void __launch_bounds__(256) k_row_merge_warp(const __grid_constant__ 
 // The streaming kernel.  Warp gw owns the flattened tiles
 // [floor(gw T / W), floor((gw+1) T / W)) of the rows * n_tiles tiles and walks
 // them in order through its ring of kStages shared-memory tile buffers: the
-// tile two ahead is in flight (bulk copy) while the current one is scanned.
+// next tile is in flight (bulk copy) while the current one is scanned, and
+// four CTAs per SM (128 registers a thread) keep 16 warps' copies going.
 // A row part closes at a row change or at the end of the range.  Warps never
 // wait for one another; the only waits are the bounded mbarrier waits on the
 // warp's own copies.
 template <typename T, int KC>
-__global__ void __launch_bounds__(kThreadsS, 3) k_sample_stream(const __grid_constant__ SampleArgs a) {
+__global__ void __launch_bounds__(kThreadsS, 4) k_sample_stream(const __grid_constant__ SampleArgs a) {
   using SMem = StreamMem<KC>;
   extern __shared__ __align__(128) unsigned char smem_stream[];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;

@@ -17,15 +17,14 @@
 
 namespace pm {
 
-constexpr int kStages = 3;
+constexpr int kStages = 2;
 
 // Per-warp shared memory of the streaming kernels.
 template <int KC>
 struct alignas(128) StreamMem {
-  // KC kept + room for several push rounds between compactions.  The extra
-  // room for KC = 64 still fits three 4-warp CTAs per SM; KC = 256 keeps
-  // +384 for the same reason.
-  static constexpr int CAP = KC == 64 ? KC + 576 : KC + 384;
+  // KC kept + room for the pushes between compactions (every 128 keys past
+  // K); with two stages a 4-warp CTA of KC = 64 takes 52 KB, four per SM
+  static constexpr int CAP = KC + 384;
   float tile[kStages][kTile];           // fp32 tile, or a bf16 tile in the first half
   uint32_t mask[kStages][32];
   uint64_t bar[kStages];
