@@ -8,8 +8,9 @@ singletons), temp 1.0, top_k 50, top_p 0.95, Philox Gumbel-max draw.
 A step is one pm_sample_rows call over one batch.  `value` is whole-job rows/s
 with inputs resident in HBM; `e2e` is the same metric through the public API
 with pinned host buffers copied in and tokens copied out inside the timed
-region.  Two input batches alternate so that no step finds its logits in L2
-(each batch is 173 MB, the L2 126 MB).
+region.  Six device-resident input batches rotate, so that no step finds the
+sectors it gathers in L2 (about 42 MB a batch; the L2 holds 126 MB), and a
+cold number with L2 flushed before every step is reported beside it.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
@@ -34,6 +35,7 @@ B_PER_GPU = 256
 VOCAB = 163840
 BYTES_PER_ROW = VOCAB * 4 + (VOCAB // 32) * 4  # logits + bitmask = 675,840 B
 LAUNCHES_PER_STEP = 1  # k_sample_masked (masked rows, no penalties, no logit bias, top_k bounded)
+N_BATCHES = 6  # device-resident input batches in rotation (see bench_config)
 WORKLOAD = ("C3: 256 rows per GPU, V=163,840 fp32 logits + packed allowed-token bitmask (~2% set), "
             "temp 1.0, top_k 50, top_p 0.95, Philox Gumbel-max draw")
 
@@ -69,16 +71,27 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def traffic_per_launch():
-    """DRAM bytes per launch from the committed ncu summary (None if absent)."""
-    path = os.path.join(ROOT, "profiles", "k_sample_masked_c3.md")
+def traffic_per_launch(kernel: str, workload: str):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum of
+    one ncu capture) from the tab-separated table profiles/dram_traffic.tsv
+    (kernel, workload, bytes per launch, source summary); None if absent."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.tsv")
     try:
         for line in open(path):
-            if line.startswith("dram_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].split()[0])
-    except OSError:
+            f = line.rstrip("\n").split("\t")
+            if len(f) >= 3 and f[0] == kernel and f[1] == workload:
+                return float(f[2])
+    except (OSError, ValueError):
         pass
     return None
+
+
+def bench_config(world: int) -> dict:
+    """The config dict both arms print for the C3 workload."""
+    return {"workload": WORKLOAD, "rows_per_gpu": B_PER_GPU, "vocab": VOCAB, "n_gpus": world,
+            "l2": f"{N_BATCHES} input batches in rotation (device-resident arm): their gathered sectors "
+                  f"(~42 MB a batch) exceed the 126 MB L2; cold_us_per_step flushes L2 before every step",
+            "noise": "Philox4x32-10"}
 
 
 class Clocks:
@@ -180,11 +193,13 @@ def cpu_baseline(d, seconds: float):
 
 
 def run_reference(args):
+    """The reference arm: the oracle port (the reference's own sampler is
+    mlx-lm over MLX, darwin-only) on all host cores, on the same C3 workload,
+    metric and config as the device arm.  Loads no library of this package:
+    the inputs come from paged_moe_b200.workloads, which is host-only."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    import numpy as np  # noqa: F401
-
     import oracle as O
     d = make_inputs(seed=0)
     s = d["sampler"]
@@ -206,14 +221,21 @@ def run_reference(args):
         "metric": METRIC, "value": val, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000 * tot / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "rows_per_step": n, "vocab": VOCAB},
+        "config": bench_config(args.gpus),
         "impl": "reference",
+        "p50_us_per_step": 1e6 * statistics.median(times),
         "cpu_baseline": {"value": val, "unit": "rows/s", "cores": cores, "kind": "port",
-                         "sample": f"{n} C3 rows per step, oracle on {cores} host threads "
+                         "sample": f"{n} C3 rows per step, {args.steps} steps, oracle port on {cores} host threads "
                                    "(the reference's MLX path is darwin-only)"},
         "e2e": {"value": val, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def l2_flush_buffer(dev):
+    """A device buffer twice the size of L2: writing it evicts every line."""
+    import torch
+    return torch.empty(64 << 20, dtype=torch.float32, device=dev)  # 256 MB
 
 
 def run_ours(args):
@@ -233,21 +255,21 @@ def run_ours(args):
         pg = dist
     import paged_moe_b200 as pm
 
-    d0 = make_inputs(seed=1000 * rank)
-    d1 = make_inputs(seed=1000 * rank + 1)
-    s = d0["sampler"]
-    xs = [torch.from_numpy(d["logits"]).to(dev) for d in (d0, d1)]
-    ms = [torch.from_numpy(d["mask"].view(np.int32)).to(dev) for d in (d0, d1)]
+    ds = [make_inputs(seed=1000 * rank + k) for k in range(N_BATCHES)]
+    s = ds[0]["sampler"]
+    xs = [torch.from_numpy(d["logits"]).to(dev) for d in ds]
+    ms = [torch.from_numpy(d["mask"].view(np.int32)).to(dev) for d in ds]
     stream = torch.cuda.current_stream(dev)
 
     def step(i):
-        return pm.sample_rows(xs[i & 1], s, mask=ms[i & 1], seed=12345, offset=i, row_base=rank * B_PER_GPU)
+        k = i % N_BATCHES
+        return pm.sample_rows(xs[k], s, mask=ms[k], seed=12345, offset=i, row_base=rank * B_PER_GPU)
 
-    for i in range(args.warmup):
+    for i in range(max(args.warmup, N_BATCHES)):
         step(i)
     torch.cuda.synchronize(dev)
-    # eager steps, one event each (reported beside the timed number: the
-    # host's issue time per call, about 25 us, sets their pace)
+    # eager steps, one event each: the latency a caller that issues one call
+    # per decode step sees (host issue time included)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     ev[0].record(stream)
     for i in range(args.steps):
@@ -255,9 +277,21 @@ def run_ours(args):
         ev[i + 1].record(stream)
     torch.cuda.synchronize(dev)
     per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    # cold steps: L2 flushed before each, events around the step alone
+    flush = l2_flush_buffer(dev)
+    cold = []
+    for i in range(min(args.steps, 20)):
+        flush.fill_(float(i))
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        step(2000 + i)
+        c1.record(stream)
+        torch.cuda.synchronize(dev)
+        cold.append(c0.elapsed_time(c1))
+    del flush
     # the timed region: the K steps captured once into a CUDA graph and
     # replayed, so the device runs them back to back; every replay recomputes
-    # every step from its inputs (two alternating batches)
+    # every step from its inputs (N_BATCHES batches in rotation)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         for i in range(args.steps):
@@ -286,11 +320,12 @@ def run_ours(args):
     value = rows_total / (ms_step / 1000.0)
 
     # end to end through the public API: pinned host logits + mask in, tokens out
-    hx = [torch.from_numpy(d["logits"]).pin_memory() for d in (d0, d1)]
-    hm = [torch.from_numpy(d["mask"].view(np.int32)).pin_memory() for d in (d0, d1)]
+    hx = [torch.from_numpy(d["logits"]).pin_memory() for d in ds[:2]]
+    hm = [torch.from_numpy(d["mask"].view(np.int32)).pin_memory() for d in ds[:2]]
     htok = torch.empty(B_PER_GPU, dtype=torch.int32).pin_memory()
-    dx = torch.empty_like(xs[0])
-    dm = torch.empty_like(ms[0])
+    del xs, ms
+    dx = torch.empty(hx[0].shape, dtype=hx[0].dtype, device=dev)
+    dm = torch.empty(hm[0].shape, dtype=hm[0].dtype, device=dev)
     e2e_steps = max(3, min(args.steps, 20))
 
     def e2e_step(i):
@@ -321,7 +356,7 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(d0, args.cpu_seconds)
+        cpu = cpu_baseline(ds[0], args.cpu_seconds)
     if pg:
         pg.barrier()
         pg.destroy_process_group()
@@ -329,29 +364,31 @@ def run_ours(args):
         return
     peak, peak_kind = peaks()
     dense_bytes = BYTES_PER_ROW * B_PER_GPU
-    bytes_launch = (gather_bytes(d0["mask"]) + gather_bytes(d1["mask"])) / 2
-    mean_launch_s = ms_step / 1000.0  # one launch per step, back to back
-    achieved = bytes_launch / mean_launch_s / 1e9
-    trf = traffic_per_launch()
+    sparse_bytes = statistics.mean(gather_bytes(d["mask"]) for d in ds)
+    launch_s = ms_step / 1000.0  # one launch per step, back to back
+    achieved = dense_bytes / launch_s / 1e9
+    trf = traffic_per_launch("k_sample_masked", "C3")
     line = {
         "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "rows_per_gpu": B_PER_GPU, "vocab": VOCAB,
-                   "l2": "two alternating input batches of 173 MB each (> 126 MB L2)",
-                   "noise": "Philox4x32-10"},
+        "config": bench_config(world),
         "timing": "CUDA graph of the K steps, replayed once (events around the replay)",
-        "eager_mean_us_per_step": 1000 * statistics.mean(per),
         "eager_p50_us_per_step": 1000 * statistics.median(per),
+        "eager_mean_us_per_step": 1000 * statistics.mean(per),
+        "cold_us_per_step": 1000 * statistics.median(cold),
         "logits_gb_per_s": achieved,
-        "dense_equivalent_gb_per_s": dense_bytes / mean_launch_s / 1e9,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": trf,
                      "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs",
-                     "algorithmic_bytes_per_launch": bytes_launch,
-                     "bytes_rule": "mask words + the 32-byte logits sectors holding an allowed token "
-                                   "(the masked pass reads nothing else); dense_equivalent_gb_per_s counts "
-                                   "the whole 675,840 B/row"},
+                     "algorithmic_bytes_per_launch": dense_bytes,
+                     "bytes_rule": "675,840 B per row (fp32 logits + packed mask) x 256 rows; the masked pass "
+                                   "reads only the mask and the 32-byte sectors holding an allowed token "
+                                   "(disallowed logits are -inf under the mask processor and change nothing)",
+                     "sparse_bytes_per_launch": sparse_bytes,
+                     "sparse_gb_per_s": sparse_bytes / launch_s / 1e9,
+                     "dram_gb_per_s": None if trf is None else trf / launch_s / 1e9,
+                     "dram_frac": None if trf is None else trf / launch_s / 1e9 / peak},
         "e2e": {"value": e2e_val, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "clocks": clocks,
@@ -456,29 +493,32 @@ def run_config(args):
     from paged_moe_b200.params import SamplerSettings
     dev = torch.device("cuda", 0)
     wl = args.workload
+    # batches in rotation: enough that one pass over them exceeds the 126 MB
+    # L2 twice (C1's 0.6 MB row is latency-bound and stays L2-resident)
+    nb = {"c1": 2, "c2": 16, "c2b": 16, "c4a": 4, "c4b": 4}[wl]
     if wl == "c1":
-        ds = [W.c1(seed=k) for k in range(2)]
+        ds = [W.c1(seed=k) for k in range(nb)]
         xs = [torch.from_numpy(d["logits"]).to(dev) for d in ds]
         hs = [torch.from_numpy(d["hist"]).to(dev) for d in ds]
         s, p = ds[0]["sampler"], ds[0]["proc"]
         rows, nbytes = 1, 151936 * 4 + 256 * 4
 
         def step(i):
-            return pm.sample_rows(xs[i & 1], s, p, history=hs[i & 1], seed=5, offset=i)
+            return pm.sample_rows(xs[i % nb], s, p, history=hs[i % nb], seed=5, offset=i)
         desc = "C1: B=1, V=151,936 fp32, temp 0.7, top_k 20, top_p 0.8, repetition 1.05 over 256 ids"
     elif wl in ("c2", "c2b"):
-        ds = [W.c2(seed=k, second=(wl == "c2b")) for k in range(2)]
+        ds = [W.c2(seed=k, second=(wl == "c2b")) for k in range(nb)]
         xs = [torch.from_numpy(d["logits_bf16"].view(np.int16)).to(dev).view(torch.bfloat16) for d in ds]
         hs = [torch.from_numpy(d["hist"]).to(dev) for d in ds]
         s, p = ds[0]["sampler"], ds[0]["proc"]
         rows, nbytes = 64, 64 * (151936 * 2 + 4096 * 4)
 
         def step(i):
-            return pm.sample_rows(xs[i & 1], s, p, history=hs[i & 1], seed=5, offset=i)
+            return pm.sample_rows(xs[i % nb], s, p, history=hs[i % nb], seed=5, offset=i)
         desc = ("C2: B=64, V=151,936 bf16, 4,096-id Zipf histories, presence 0.5 + frequency 0.3, "
                 + ("min_p 0.05 at temp 1" if wl == "c2b" else "argmax"))
     else:
-        ds = [W.c4(seed=k) for k in range(2)]
+        ds = [W.c4(seed=k) for k in range(nb)]
         tg = [torch.from_numpy(d["target"]).to(dev) for d in ds]
         dl = [torch.from_numpy(d["draft_logits"]).to(dev) for d in ds]
         dr = [torch.from_numpy(d["drafts"]).to(dev) for d in ds]
@@ -491,7 +531,7 @@ def run_config(args):
         nbytes = 32 * (5 + (4 if resid else 0)) * 151552 * 4
 
         def step(i):
-            k = i & 1
+            k = i % nb
             if resid:
                 return pm.verify(tg[k], dr[k], yy[k], s, mode="residual", draft_logits=dl[k], u_accept=ua[k],
                                  u_residual=ur[k], seed=5, offset=i)
@@ -512,9 +552,10 @@ def run_config(args):
         torch.cuda.synchronize(dev)
     per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
     # the same steps replayed from a CUDA graph (no host work between them)
+    ng = max(8, nb)  # every batch once per replay
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        for i in range(8):
+        for i in range(ng):
             step(1000 + i)
     g.replay()
     torch.cuda.synchronize(dev)
@@ -524,7 +565,7 @@ def run_config(args):
         g.replay()
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    graph_us = e0.elapsed_time(e1) * 1000 / 32
+    graph_us = e0.elapsed_time(e1) * 1000 / (4 * ng)
     del g
     peak, peak_kind = peaks()
     ms = statistics.mean(per)
@@ -532,8 +573,8 @@ def run_config(args):
         "metric": f"sampled rows/s ({wl.upper()}); p50 us/step", "value": rows / (ms / 1000.0), "unit": "rows/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": desc},
-        "p50_us_per_step": 1000 * statistics.median(per),
+        "config": {"workload": desc, "l2": f"{nb} input batches in rotation"},
+        "eager_p50_us_per_step": 1000 * statistics.median(per),
         "graph_us_per_step": graph_us,
         "roofline": {"bound": "hbm", "achieved": nbytes / (graph_us * 1e-6) / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": nbytes / (graph_us * 1e-6) / 1e9 / peak, "traffic": None,

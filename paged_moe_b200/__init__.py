@@ -6,20 +6,25 @@ Public API:
     verify                                  draft acceptance of a verify pass
     sampling                                request defaults (pagedmoe/sampling.py)
 
-Importing this package loads libpm_sample.so; there is no CPU path.
+The CUDA library (libpm_sample.so) is loaded on the first call that launches
+work, so host-only modules (settings, request defaults, synthetic workloads)
+import without it.  There is no CPU path: that first call raises ImportError
+when the library is missing or does not load.
 """
 
 from . import _lib
 from . import sampling  # noqa: F401  (host-side defaults, pure Python)
 from .params import ProcessorSettings, SamplerSettings  # noqa: F401
-
-_lib.load()
-
 from .engine import apply_processors, argmax_confidence, logprobs, sample_rows  # noqa: E402,F401
 from .sample_utils import make_logits_processors, make_sampler  # noqa: E402,F401
 from .verify import verify  # noqa: E402,F401
 
-__version__ = "0.1.0"
+__version__ = "0.2.0"
+
+
+def load_library():
+    """Load libpm_sample.so now (building it first when nvcc is present)."""
+    return _lib.load()
 
 
 def library_path() -> str:

@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 SO = os.path.join(HERE, "libpm_sample.so")
-SOURCES = ["pm_sample.cu", "pm_verify.cu", "pm_shard.cu"]
+SOURCES = ["pm_sample.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

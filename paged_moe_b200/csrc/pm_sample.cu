@@ -17,6 +17,7 @@
 // the draw.
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "pm_device.cuh"
@@ -31,6 +32,11 @@ namespace pm {
 
 constexpr int kWarpsS = 4;                 // warps per CTA of the streaming kernel
 constexpr int kThreadsS = kWarpsS * 32;
+// Streaming CTAs resident per SM: four at KC = 64 (51.6 KB of shared memory
+// each, so 128 registers a thread), three at KC = 256 (57.8 KB each: a
+// fourth would not fit in 228 KB, so its registers need no tighter cap).
+template <int KC>
+constexpr int kStreamBlocks = KC == 64 ? 4 : 3;
 
 // Per-row state of a warp's current row part.
 struct PartState {
@@ -690,7 +696,7 @@ __global__ void __launch_bounds__(256) k_row_merge_warp(const __grid_constant__ 
 // wait for one another; the only waits are the bounded mbarrier waits on the
 // warp's own copies.
 template <typename T, int KC>
-__global__ void __launch_bounds__(kThreadsS, 4) k_sample_stream(const __grid_constant__ SampleArgs a) {
+__global__ void __launch_bounds__(kThreadsS, kStreamBlocks<KC>) k_sample_stream(const __grid_constant__ SampleArgs a) {
   using SMem = StreamMem<KC>;
   extern __shared__ __align__(128) unsigned char smem_stream[];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -879,34 +885,80 @@ bool penalties_on(const pm_rows* r) {
   return r->hist && (r->flags_any & (PM_F_REP | PM_F_PRES | PM_F_FREQ));
 }
 
-int num_sms() {
-  static int sms = 0;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
-      cudaGetLastError();
-      sms = 148;
+constexpr int kMaxDevices = 64;
+
+int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) {
+    cudaGetLastError();
+    d = 0;
+  }
+  return d;
+}
+
+// One-time setup per device: kernel attributes (the dynamic shared memory
+// limit) and occupancy queries belong to the device that is current, so a
+// process that drives several GPUs repeats them on each.
+class DeviceOnce {
+ public:
+  template <class F>
+  void operator()(F&& f) {
+    const int d = current_device();
+    if (d < 0 || d >= kMaxDevices) {
+      f();
+      return;
     }
+    if (done_[d].load(std::memory_order_acquire)) return;
+    std::lock_guard<std::mutex> g(mu_);
+    if (!done_[d].load(std::memory_order_relaxed)) {
+      f();
+      done_[d].store(true, std::memory_order_release);
+    }
+  }
+
+ private:
+  std::mutex mu_;
+  std::atomic<bool> done_[kMaxDevices] = {};
+};
+
+int num_sms() {
+  static int sms[kMaxDevices] = {};
+  static DeviceOnce once;
+  const int d = current_device();
+  int* slot = (d >= 0 && d < kMaxDevices) ? &sms[d] : nullptr;
+  int local = 0;
+  once([&] {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d) != cudaSuccess || v <= 0) {
+      cudaGetLastError();
+      v = 148;
+    }
+    if (slot) *slot = v;
+    local = v;
   });
-  return sms;
+  return slot ? *slot : (local ? local : 148);
 }
 
 template <typename T, int KC>
 int stream_occupancy() {
-  static int occ = 0;
-  static std::once_flag once;
-  std::call_once(once, [] {
+  static int occ[kMaxDevices] = {};
+  static DeviceOnce once;
+  const int d = current_device();
+  int* slot = (d >= 0 && d < kMaxDevices) ? &occ[d] : nullptr;
+  int local = 0;
+  once([&] {
     const size_t smem = sizeof(pm::StreamMem<KC>) * pm::kWarpsS;
     cudaFuncSetAttribute(pm::k_sample_stream<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, pm::k_sample_stream<T, KC>, pm::kThreadsS, smem) !=
-            cudaSuccess || occ < 1) {
+    int v = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, pm::k_sample_stream<T, KC>, pm::kThreadsS, smem) !=
+            cudaSuccess || v < 1) {
       cudaGetLastError();
-      occ = 4;
+      v = pm::kStreamBlocks<KC>;
     }
+    if (slot) *slot = v;
+    local = v;
   });
-  return occ;
+  return slot ? *slot : (local ? local : pm::kStreamBlocks<KC>);
 }
 
 int occupancy_for(int dtype, int KC) {
@@ -1036,8 +1088,8 @@ int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::Sample
     pa.status = a.status;
     pa.row_tau = a.row_tau;
     const size_t smem = sizeof(int) * (6 * (size_t)L.ovr_cap + 2 * 264);
-    static std::once_flag once;
-    std::call_once(once, [] {
+    static DeviceOnce once;
+    once([&] {
       cudaFuncSetAttribute(pm::k_prep_overrides, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * (6 * 8192 + 2 * 264));
     });
     pm::k_prep_overrides<<<(unsigned)r->rows, 1024, smem, st>>>(pa);
@@ -1105,8 +1157,8 @@ int launch_stream(const pm::SampleArgs& a, bool cand_rows, cudaStream_t st, bool
   // otherwise
   const bool per_cta = a.rows <= (int64_t)num_sms() * 2;
   const size_t msmem = per_cta ? sizeof(pm::MergeCta<KC>) : (sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * 8;
-  static std::once_flag once;
-  std::call_once(once, [] {
+  static DeviceOnce once;
+  once([&] {
     cudaFuncSetAttribute(pm::k_row_merge_cta<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)sizeof(pm::MergeCta<KC>));
     cudaFuncSetAttribute(pm::k_row_merge_warp<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1154,8 +1206,8 @@ bool masked_path(const pm_rows* r) {
 template <typename T, int KC>
 int launch_masked(const pm::SampleArgs& a, cudaStream_t st) {
   const size_t smem = sizeof(pm::MaskedMem<KC>);
-  static std::once_flag once;
-  std::call_once(once, [smem] {
+  static DeviceOnce once;
+  once([&] {
     cudaFuncSetAttribute(pm::k_sample_masked<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   });
   int64_t grid = a.rows;
@@ -1168,8 +1220,8 @@ int launch_masked(const pm::SampleArgs& a, cudaStream_t st) {
 template <typename T>
 int launch_wide(const pm::SampleArgs& a, cudaStream_t st) {
   const size_t smem = sizeof(pm::WideMem);
-  static std::once_flag once;
-  std::call_once(once, [smem] {
+  static DeviceOnce once;
+  once([&] {
     cudaFuncSetAttribute(pm::k_row_wide<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   });
   int64_t grid = a.rows;
@@ -1563,8 +1615,8 @@ template <typename T, int KC>
 int launch_shard_pack(const pm::SampleArgs& a, const pm::ShardK& sk, cudaStream_t st) {
   constexpr int kWarpsP = 8;
   const size_t smem = (sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * kWarpsP;
-  static std::once_flag once;
-  std::call_once(once, [smem] {
+  static DeviceOnce once;
+  once([&] {
     cudaFuncSetAttribute(pm::k_shard_pack<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   });
   int64_t grid = (a.rows + kWarpsP - 1) / kWarpsP;
@@ -1607,8 +1659,8 @@ template <int KC>
 int launch_shard_merge(const pm::SampleArgs& a, const pm::MergeK& m, cudaStream_t st) {
   constexpr int kWarpsM = 8;
   const size_t smem = (sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * kWarpsM;
-  static std::once_flag once;
-  std::call_once(once, [smem] {
+  static DeviceOnce once;
+  once([&] {
     cudaFuncSetAttribute(pm::k_shard_merge<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   });
   int64_t grid = (a.rows + kWarpsM - 1) / kWarpsM;
@@ -1779,7 +1831,6 @@ namespace {
 
 static __device__ __align__(256) unsigned char g_static_scratch[PM_STATIC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
 std::mutex g_static_mu;
 void* g_static_ptr[kMaxDevices] = {};
 

@@ -51,6 +51,14 @@ __device__ __forceinline__ bool cand_offer_vec(const float (&x)[VW], float lmax,
                                                unsigned* hist, Cand& c, int K) {
   const int lane = threadIdx.x & 31;
   if (!__any_sync(kFull, lmax > -INFINITY && lmax >= c.tau_x)) return false;
+  // room for the 32 * VW keys this call may append: another offer routine
+  // (one value per lane, or a narrower vector) can have left the buffer
+  // fuller than this routine's own compaction bound
+  bool compacted = false;
+  if (c.cnt > CAP - 32 * VW) {
+    cand_compact<CAP>(buf, hist, c, K);
+    compacted = true;
+  }
   const unsigned below = (1u << lane) - 1u;
   int base = c.cnt;
 #pragma unroll
@@ -69,7 +77,7 @@ __device__ __forceinline__ bool cand_offer_vec(const float (&x)[VW], float lmax,
     cand_compact<CAP>(buf, hist, c, K);
     return true;
   }
-  return false;
+  return compacted;
 }
 
 // Offer one value per lane (token tok) to the buffer: appended when its key

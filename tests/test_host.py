@@ -77,3 +77,19 @@ def test_factories_keep_mlx_lm_signatures():
         SU.make_sampler(temp=1.0, xtc_probability=0.5)
     s = SU.make_sampler(temp=0.7, top_p=0.9, seed=5)
     assert s.settings == P.SamplerSettings(temp=0.7, top_p=0.9) and s.seed == 5
+
+
+def test_import_and_workloads_load_no_product_library():
+    """The package and its synthetic workloads import without loading
+    libpm_sample.so (the benchmark's reference arm builds its inputs from
+    them and must run none of this package's native code)."""
+    import subprocess
+    import sys
+    code = ("import paged_moe_b200, paged_moe_b200.workloads as W\n"
+            "W.c3(seed=0, B=2, V=4096)\n"
+            "maps = open('/proc/self/maps').read()\n"
+            "print('LOADED' if 'libpm_sample' in maps else 'CLEAN')\n")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300,
+                         cwd=__import__("os").path.dirname(__import__("os").path.dirname(__file__)))
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip().endswith("CLEAN"), out.stdout
