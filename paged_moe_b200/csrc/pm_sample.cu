@@ -492,7 +492,7 @@ __device__ __forceinline__ void part_end(const SampleArgs& a, int64_t row, int64
 // Row outputs (lane 0).
 __device__ __forceinline__ void write_row(const SampleArgs& a, int64_t row, int mode, int tok, float x_tok,
                                           float lse, int ns) {
-  const int32_t prevs = a.prep_ran ? ld_cg(&a.status[row]) : 0;
+  const int32_t prevs = a.status_live ? ld_cg(&a.status[row]) : 0;
   a.status[row] = prevs | (tok < 0 ? 1 : 0);
   a.tokens[row] = tok;
   if (a.lse_out) a.lse_out[row] = lse;
@@ -1064,7 +1064,7 @@ int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::Sample
   a.bias_tok = nullptr;
   a.bias_val = nullptr;
   a.bias_off = nullptr;
-  a.prep_ran = false;
+  a.status_live = false;
   a.feed_group = r->feed ? r->feed_group : 0;
   a.verify = nullptr;
   cudaError_t e;
@@ -1098,7 +1098,7 @@ int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::Sample
     a.ovr_tok = pa.ovr_tok;
     a.ovr_info = pa.ovr_info;
     a.ovr_off = pa.ovr_off;
-    a.prep_ran = true;
+    a.status_live = true;
   }
   if (r->n_bias > 0) {
     a.bias_tok = r->bias_tokens;
@@ -1117,17 +1117,28 @@ bool has_cand_rows(const pm_rows* r) {
 }
 
 template <typename T, int KC>
-int launch_stream(const pm::SampleArgs& a, bool cand_rows, cudaStream_t st, bool merge = true) {
+int launch_stream(pm::SampleArgs a, bool cand_rows, cudaStream_t st, bool merge = true) {
   stream_occupancy<T, KC>();
   const size_t smem = sizeof(pm::StreamMem<KC>) * pm::kWarpsS;
   const int64_t grid = (a.n_warps + pm::kWarpsS - 1) / pm::kWarpsS;
   if (grid == 0) return PM_OK;
   cudaError_t e;
-  // the shared row thresholds start at zero ("nothing proven"); the penalty
-  // prep zeroes them when it runs
-  if (cand_rows && !a.prep_ran) {
-    e = cudaMemsetAsync(a.row_tau, 0, sizeof(uint64_t) * a.rows, st);
+  // the row status (the streaming pass ORs a copy timeout into it) and the
+  // shared row thresholds ("nothing proven") start at zero; the penalty prep
+  // zeroes both when it runs.  The workspace plan puts the thresholds right
+  // after the status array, so one memset covers both.
+  if (!a.status_live) {
+    const char* s0 = reinterpret_cast<const char*>(a.status);
+    const char* t0 = reinterpret_cast<const char*>(a.row_tau);
+    const size_t sb = sizeof(int32_t) * a.rows, tb = sizeof(uint64_t) * a.rows;
+    if (cand_rows && t0 >= s0 + sb && t0 <= s0 + sb + 256) {
+      e = cudaMemsetAsync(a.status, 0, (size_t)(t0 - s0) + tb, st);
+    } else {
+      e = cudaMemsetAsync(a.status, 0, sb, st);
+      if (e == cudaSuccess && cand_rows) e = cudaMemsetAsync(a.row_tau, 0, tb, st);
+    }
     if (e != cudaSuccess) return cuda_fail(e);
+    a.status_live = true;
   }
   {
     // programmatic dependent launch: the tile prologue overlaps the tail of

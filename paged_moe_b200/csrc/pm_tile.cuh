@@ -63,7 +63,7 @@ struct SampleArgs {
   uint64_t* best;    // [rows, max_parts] greedy best key of each row part
   uint64_t* row_tau;   // [rows] largest K-th key any part of the row has proven (0: none)
   int32_t* status;   // [rows] 0 ok, 1 survivors beyond the candidates, 2 history window too long
-  bool prep_ran;     // the override prep wrote status this call
+  bool status_live;  // status[] already holds this call's flags (zeroed, or written by the penalty prep)
   float* row_lse;    // [rows]
   int32_t n_tiles;
   int32_t max_parts;

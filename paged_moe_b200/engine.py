@@ -245,8 +245,9 @@ def status_view(ws: torch.Tensor, r: L.Rows) -> torch.Tensor:
 
 
 def apply_processors(logits: torch.Tensor, processors=None, history=None, history_len=None, mask=None,
-                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Processed logits (fp32): logit bias, penalties, then the mask."""
+                     out: Optional[torch.Tensor] = None, return_status: bool = False):
+    """Processed logits (fp32): logit bias, penalties, then the mask.  With
+    return_status, (logits, per-row status [B] int32)."""
     keep = _Keep()
     lib = L.load()
     dev = logits.device
@@ -259,6 +260,10 @@ def apply_processors(logits: torch.Tensor, processors=None, history=None, histor
     rc = lib.pm_apply_processors(C.byref(r), out.data_ptr(), out.stride(0), ws.data_ptr(), ws.numel(),
                                  stream.cuda_stream)
     L.check(rc, "pm_apply_processors")
+    if return_status:
+        # the status array opens the workspace; only the penalty prep writes it
+        st = status_view(ws, r) if r.hist else torch.zeros(r.rows, dtype=torch.int32, device=dev)
+        return out, st
     return out
 
 

@@ -12,52 +12,100 @@ logits-processor call shape for single rows.
 
 from __future__ import annotations
 
-from typing import Optional, Sequence
+from typing import Dict, List, Optional, Sequence, Tuple
 
+import numpy as np
 import torch
 
 from . import _lib as L
 
-SLACK_TOKENS = 48  # reference think_budget.py:36
-_ENDS = (".", "!", "?", ":", "\n")  # reference think_budget.py:37
-_TABLES: dict = {}
+SLACK_TOKENS = 48  # tokens to wait for a sentence end past the budget (reference think_budget.py:36)
+# characters that end a sentence when a decoded piece ends with one of them
+# (trailing spaces ignored; reference think_budget.py:37)
+_SENTENCE_END = frozenset(".!?:\n")
+_DECODE_CHUNK = 8192
+
+
+class PieceTables:
+    """Per-id tables of one tokenizer on one device: how many characters the
+    id decodes to, and whether that piece ends a sentence.  Decoding the
+    whole vocabulary takes a while (about half a second for 250k ids), so
+    the tables are made once per (tokenizer, device) and shared."""
+
+    _cache: Dict[Tuple[int, str], "PieceTables"] = {}
+
+    def __init__(self, lens: torch.Tensor, ends: torch.Tensor):
+        self.lens, self.ends = lens, ends
+
+    @classmethod
+    def of(cls, tokenizer, device) -> "PieceTables":
+        key = (id(tokenizer), str(device))
+        hit = cls._cache.get(key)
+        if hit is None:
+            lens, ends = cls._build(tokenizer)
+            hit = cls(torch.from_numpy(lens).to(device), torch.from_numpy(ends).to(device))
+            cls._cache[key] = hit
+        return hit
+
+    @staticmethod
+    def _pieces(tokenizer, lo: int, hi: int) -> List[str]:
+        ids = [[i] for i in range(lo, hi)]
+        try:
+            return list(tokenizer.batch_decode(ids))
+        except Exception:  # a tokenizer without a batched decode (or one that refuses an id list)
+            return [tokenizer.decode(i) for i in range(lo, hi)]
+
+    @classmethod
+    def _build(cls, tokenizer):
+        n = max(tokenizer.get_vocab().values()) + 1
+        lens = np.zeros(n, dtype=np.int32)
+        ends = np.zeros(n, dtype=np.uint8)
+        for lo in range(0, n, _DECODE_CHUNK):
+            hi = min(n, lo + _DECODE_CHUNK)
+            for off, piece in enumerate(cls._pieces(tokenizer, lo, hi)):
+                lens[lo + off] = len(piece)
+                tail = piece.rstrip(" ")
+                ends[lo + off] = bool(tail) and tail[-1] in _SENTENCE_END
+        return lens, ends
 
 
 def piece_tables(tokenizer, device) -> tuple:
-    """Decoded length and sentence-end flag per id, built once per tokenizer."""
-    key = (id(tokenizer), str(device))
-    got = _TABLES.get(key)
-    if got is not None:
-        return got
-    n = max(tokenizer.get_vocab().values()) + 1
-    ids = [[i] for i in range(n)]
-    try:
-        pieces = tokenizer.batch_decode(ids)
-    except Exception:
-        pieces = [tokenizer.decode(i) for i in ids]
-    lens = torch.tensor([len(p) for p in pieces], dtype=torch.int32, device=device)
-    ends = torch.tensor([p.rstrip(" ").endswith(_ENDS) for p in pieces], dtype=torch.uint8, device=device)
-    _TABLES[key] = (lens, ends)
-    return lens, ends
+    """(decoded length, sentence-end flag) per id, as device tensors."""
+    t = PieceTables.of(tokenizer, device)
+    return t.lens, t.ends
+
+
+def _close_sequence(tokenizer, close: str, end_id: int) -> List[int]:
+    """The ids the budget forces, one per step: the close text's encoding,
+    which must finish on the think end tag (otherwise forcing it would never
+    close the block)."""
+    ids = list(tokenizer.encode(close, add_special_tokens=False))
+    if not ids or ids[-1] != end_id:
+        raise ValueError(f"the close text must encode to ids ending with the think end id {end_id}, got {ids}")
+    return ids
 
 
 class ThinkBudget:
+    """Closes a reasoning block once it passes `chars` characters: after the
+    next sentence end (or `slack` tokens), the close text is forced one token
+    per step.  With `open_in_prompt` the template opened the block in the
+    prompt and every generated token counts; otherwise counting starts after
+    the model's own think start token, and a reply without one is left
+    alone."""
+
     def __init__(self, tokenizer, chars: int, close: str, open_in_prompt: bool = True, device=None,
                  slack: int = SLACK_TOKENS):
-        self.device = torch.device(device) if device is not None else torch.device("cuda")
+        self.device = torch.device("cuda" if device is None else device)
         self.chars = int(chars)
+        self.slack = int(slack)
         self.open_in_prompt = bool(open_in_prompt)
         self.end_id = int(tokenizer.think_end_id)
-        start = getattr(tokenizer, "think_start_id", None)
-        self.start_id = int(start) if start is not None else -1
-        ids = tokenizer.encode(close, add_special_tokens=False)
-        if not ids or ids[-1] != self.end_id:
-            raise ValueError("close text must end with the think end tag")
-        self.close_ids = list(ids)
-        self.close = torch.tensor(ids, dtype=torch.int32, device=self.device)
-        self.slack = int(slack)
-        self.base: Optional[int] = None
+        start = getattr(tokenizer, "think_start_id", None)  # absent: the template has no start tag
+        self.start_id = -1 if start is None else int(start)
+        self.close_ids = _close_sequence(tokenizer, close, self.end_id)
+        self.close = torch.tensor(self.close_ids, dtype=torch.int32, device=self.device)
         self.lens, self.ends = piece_tables(tokenizer, self.device)
+        self.base: Optional[int] = None  # sequence length at the first call (the prompt's tail)
 
     def forced(self, gen: torch.Tensor, gen_len: Optional[torch.Tensor] = None,
                chars: Optional[Sequence[int]] = None) -> torch.Tensor:
