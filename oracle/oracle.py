@@ -20,7 +20,7 @@ from typing import Optional, Sequence
 import numpy as np
 
 __all__ = [
-    "lib", "build", "Proc", "Sampler", "expf", "q52", "exp64", "log64", "philox4x32_10",
+    "lib", "build", "Proc", "Sampler", "expf", "expf_shift", "q52", "exp64", "log64", "philox4x32_10",
     "gumbel_from_word", "u53", "row_lse", "tile_stats", "process", "logprobs", "sample",
     "verify", "bf16_to_f32", "philox_gumbel", "philox_uniform", "window_start",
     "shard_sample", "draft_ngram",
@@ -98,6 +98,8 @@ def lib():
             L.orc_logprobs_batch.argtypes = common + [P, P]
             L.orc_process_batch.restype = C.c_int
             L.orc_process_batch.argtypes = common + [P]
+            L.orc_expf_shift.restype = None
+            L.orc_expf_shift.argtypes = [P, C.c_int, C.c_float, P]
             _lib = L
     return _lib
 
@@ -178,6 +180,14 @@ class Sampler:
 
 def expf(d: float) -> float:
     return lib().orc_expf(d)
+
+
+def expf_shift(x: np.ndarray, c: float) -> np.ndarray:
+    """expf(fl32(x - c)) of every element (the scalar expf, vectorised in C)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    lib().orc_expf_shift(_p(x), x.size, float(np.float32(c)), _p(out))
+    return out
 
 
 def q52(d: float) -> int:
@@ -477,12 +487,12 @@ def verify(target, drafts, y, sampler: Sampler, mode: str = "match", draft_logit
             inv = np.float32(1.0 / sc.temp)
             yv = np.where(np.isfinite(x), x * inv, np.float32(-np.inf)).astype(np.float32)
             ly = np.float32(row_lse(yv))
-            return np.array([expf(float(np.float32(v - ly))) for v in yv], dtype=np.float32)
+            return expf_shift(yv, ly)
 
         def q_row(i):
             d = dl[i]
             c = np.float32(row_lse(d))
-            return np.array([expf(float(np.float32(v - c))) for v in d], dtype=np.float32)
+            return expf_shift(d, c)
 
         out = []
         rejected = -1
@@ -496,8 +506,10 @@ def verify(target, drafts, y, sampler: Sampler, mode: str = "match", draft_logit
                 continue
             rejected = i
             r = np.maximum(p - q, np.float32(0.0)).astype(np.float32)
-            qr = np.array([int(np.float64(v) * 2.0 ** 52) for v in r], dtype=np.uint64)
-            R = int(qr.sum(dtype=np.uint64))
+            # floor(r 2^52) exactly: r <= 1, so the product is exact in fp64
+            qr = (r.astype(np.float64) * 2.0 ** 52).astype(np.uint64)
+            cum = np.cumsum(qr, dtype=np.uint64)  # the residual mass is at most ~1: no overflow
+            R = int(cum[-1]) if V else 0
             if R == 0:
                 out.append(draw(i)[0])
             else:
@@ -505,14 +517,9 @@ def verify(target, drafts, y, sampler: Sampler, mode: str = "match", draft_logit
                         else philox_uniform(seed, offset, b * K1 + i, 3))
                 u53v = min(int(float(ures) * 2.0 ** 53), 2 ** 53 - 1) if ures > 0 else 0
                 tgt = (u53v * R) >> 53
-                acc = 0
-                tok = V - 1
-                for v in range(V):
-                    acc += int(qr[v])
-                    if acc > tgt:
-                        tok = v
-                        break
-                out.append(tok)
+                # the first id whose inclusive prefix exceeds tgt
+                tok = int(np.searchsorted(cum, np.uint64(tgt), side="right"))
+                out.append(tok if tok < V else V - 1)
             break
         if rejected < 0:
             out.append(draw(k)[0])

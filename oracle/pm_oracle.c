@@ -653,3 +653,14 @@ int orc_process_batch(const float *logits, int B, int V, const int32_t *hist, in
     }
     return ORC_OK;
 }
+
+/* Vector form used by the residual-mode restatement: out[i] =
+ * orc_expf(fl32(x[i] - c)) (0 for x[i] = -inf), the probabilities
+ * expf(y - lse(y)) of a whole row in one call. */
+void orc_expf_shift(const float *x, int n, float c, float *out)
+{
+    for (int i = 0; i < n; ++i) {
+        const float d = x[i] - c;
+        out[i] = orc_expf(d);
+    }
+}

@@ -96,3 +96,13 @@ def test_full_draw_is_the_softmax(V):
     exp = n * p[top]
     chi2 = float(((obs - exp) ** 2 / exp).sum())
     assert chi2 < 40.0, (chi2, obs, exp)
+
+
+def test_expf_shift_is_the_scalar_expf():
+    import numpy as np
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(2000).astype(np.float32) * 20, [-np.inf, 0.0]]).astype(np.float32)
+    c = np.float32(1.25)
+    got = O.expf_shift(x, c)
+    want = np.array([O.expf(float(np.float32(v - c))) for v in x], dtype=np.float32)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
