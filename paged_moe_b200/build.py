@@ -15,7 +15,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 SO = os.path.join(HERE, "libpm_sample.so")
-SOURCES = ["pm_sample.cu"]
+SOURCES = ["pm_sample.cu", "pm_masked.cu"]
+OBJDIR = os.path.join(HERE, "_build")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -37,27 +38,50 @@ def sources() -> list:
     return [os.path.join(CSRC, s) for s in SOURCES if os.path.exists(os.path.join(CSRC, s))]
 
 
+def _headers() -> list:
+    hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
+    return hs + [os.path.join(ROOT, "include", "pm_sample.h")]
+
+
 def _stale() -> bool:
     if not os.path.exists(SO):
         return True
     t = os.path.getmtime(SO)
-    deps = sources() + [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cuh")]
-    deps.append(os.path.join(ROOT, "include", "pm_sample.h"))
-    return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
+    return any(os.path.getmtime(d) > t for d in sources() + _headers() if os.path.exists(d))
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile every translation unit (in parallel) and link the library."""
     if not force and not _stale():
         return SO
-    cmd = [nvcc(), *NVCC_FLAGS, "-shared", "-o", SO + ".tmp", *sources(), "-lcudart"]
-    if verbose:
-        print(" ".join(cmd), flush=True)
+    os.makedirs(OBJDIR, exist_ok=True)
+    cc = nvcc()
+    procs = []
+    objs = []
+    for src in sources():
+        obj = os.path.join(OBJDIR, os.path.basename(src) + ".o")
+        objs.append(obj)
+        cmd = [cc, *NVCC_FLAGS, "-c", "-o", obj + ".tmp", src]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        procs.append((obj, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)))
+    failed = False
+    for obj, pr in procs:
+        out, _ = pr.communicate()
+        if pr.returncode != 0:
+            sys.stderr.write(out)
+            failed = True
+        else:
+            if verbose and out:
+                sys.stderr.write(out)
+            os.replace(obj + ".tmp", obj)
+    if failed:
+        raise RuntimeError("nvcc failed building libpm_sample.so")
+    cmd = [cc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", SO + ".tmp", *objs, "-lcudart"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)
-        raise RuntimeError("nvcc failed building libpm_sample.so")
-    if verbose and (res.stdout or res.stderr):
-        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError("linking libpm_sample.so failed")
     os.replace(SO + ".tmp", SO)
     return SO
 

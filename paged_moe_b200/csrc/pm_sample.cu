@@ -27,6 +27,7 @@
 #include "pm_warp.cuh"
 #include "pm_stream.cuh"
 #include "../../include/pm_sample.h"
+#include "pm_host.h"
 
 namespace pm {
 
@@ -489,18 +490,6 @@ __device__ __forceinline__ void part_end(const SampleArgs& a, int64_t row, int64
   __syncwarp();
 }
 
-// Row outputs (lane 0).
-__device__ __forceinline__ void write_row(const SampleArgs& a, int64_t row, int mode, int tok, float x_tok,
-                                          float lse, int ns) {
-  const int32_t prevs = a.status_live ? ld_cg(&a.status[row]) : 0;
-  a.status[row] = prevs | (tok < 0 ? 1 : 0);
-  a.tokens[row] = tok;
-  if (a.lse_out) a.lse_out[row] = lse;
-  if (a.row_lse) a.row_lse[row] = lse;
-  if (a.tok_logprob) a.tok_logprob[row] = tok >= 0 ? fsub(x_tok, lse) : __int_as_float(0x7fc00000);
-  if (a.n_surv && (mode != kCand || !a.surv_ids)) a.n_surv[row] = mode == kCand ? ns : 0;
-}
-
 // Merge of every row's parts: one CTA (8 warps) per row.  Launched after
 // the streaming kernel on the same stream (programmatic dependent launch: it
 // may start while the streaming kernel drains, and waits for its results).
@@ -854,7 +843,6 @@ __global__ void k_bias_offsets(const int32_t* tok, int n, int n_tiles, int32_t* 
 
 }  // namespace pm
 
-#include "pm_masked.cuh"
 #include "pm_wide.cuh"
 #include "pm_verify_impl.cuh"
 #include "pm_shard_impl.cuh"
@@ -866,12 +854,11 @@ __global__ void k_bias_offsets(const int32_t* tok, int n, int n_tiles, int32_t* 
 // ============================================================================
 namespace {
 
-thread_local int g_last_cuda = 0;
-
-int cuda_fail(cudaError_t e) {
-  g_last_cuda = (int)e;
-  return PM_ERR_CUDA;
-}
+using pmh::cuda_fail;
+using pmh::current_device;
+using pmh::DeviceOnce;
+using pmh::kMaxDevices;
+using pmh::num_sms;
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -883,60 +870,6 @@ int pow2_at_least(int64_t x) {
 
 bool penalties_on(const pm_rows* r) {
   return r->hist && (r->flags_any & (PM_F_REP | PM_F_PRES | PM_F_FREQ));
-}
-
-constexpr int kMaxDevices = 64;
-
-int current_device() {
-  int d = 0;
-  if (cudaGetDevice(&d) != cudaSuccess) {
-    cudaGetLastError();
-    d = 0;
-  }
-  return d;
-}
-
-// One-time setup per device: kernel attributes (the dynamic shared memory
-// limit) and occupancy queries belong to the device that is current, so a
-// process that drives several GPUs repeats them on each.
-class DeviceOnce {
- public:
-  template <class F>
-  void operator()(F&& f) {
-    const int d = current_device();
-    if (d < 0 || d >= kMaxDevices) {
-      f();
-      return;
-    }
-    if (done_[d].load(std::memory_order_acquire)) return;
-    std::lock_guard<std::mutex> g(mu_);
-    if (!done_[d].load(std::memory_order_relaxed)) {
-      f();
-      done_[d].store(true, std::memory_order_release);
-    }
-  }
-
- private:
-  std::mutex mu_;
-  std::atomic<bool> done_[kMaxDevices] = {};
-};
-
-int num_sms() {
-  static int sms[kMaxDevices] = {};
-  static DeviceOnce once;
-  const int d = current_device();
-  int* slot = (d >= 0 && d < kMaxDevices) ? &sms[d] : nullptr;
-  int local = 0;
-  once([&] {
-    int v = 0;
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d) != cudaSuccess || v <= 0) {
-      cudaGetLastError();
-      v = 148;
-    }
-    if (slot) *slot = v;
-    local = v;
-  });
-  return slot ? *slot : (local ? local : 148);
 }
 
 template <typename T, int KC>
@@ -1214,20 +1147,6 @@ bool masked_path(const pm_rows* r) {
   return ((uintptr_t)r->logits % 4 == 0) && (r->row_stride % 2 == 0);
 }
 
-template <typename T, int KC>
-int launch_masked(const pm::SampleArgs& a, cudaStream_t st) {
-  const size_t smem = sizeof(pm::MaskedMem<KC>);
-  static DeviceOnce once;
-  once([&] {
-    cudaFuncSetAttribute(pm::k_sample_masked<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  });
-  int64_t grid = a.rows;
-  if (grid > (int64_t)num_sms() * 2) grid = (int64_t)num_sms() * 2;
-  pm::k_sample_masked<T, KC><<<(unsigned)grid, pm::kMThreads, smem, st>>>(a);
-  const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? PM_OK : cuda_fail(e);
-}
-
 template <typename T>
 int launch_wide(const pm::SampleArgs& a, cudaStream_t st) {
   const size_t smem = sizeof(pm::WideMem);
@@ -1249,8 +1168,7 @@ int launch_rows(const pm_rows* r, int KC, const pm::SampleArgs& a, cudaStream_t 
   const bool bf = r->dtype == PM_DTYPE_BF16;
   int rc;
   if (masked_path(r)) {
-    if (KC == 64) rc = bf ? launch_masked<__nv_bfloat16, 64>(a, st) : launch_masked<float, 64>(a, st);
-    else rc = bf ? launch_masked<__nv_bfloat16, 256>(a, st) : launch_masked<float, 256>(a, st);
+    rc = pm_launch_masked(r->dtype, KC, a, st);
   } else {
     rc = launch_stream_any(r->dtype, KC, a, has_cand_rows(r), st);
   }
@@ -1373,7 +1291,7 @@ int launch_accept(const pm::SampleArgs& a, int dtype, const pm::VerifyK& vk, int
 
 extern "C" {
 
-int pm_last_cuda_error(void) { return g_last_cuda; }
+int pm_last_cuda_error(void) { return pmh::last_cuda(); }
 
 const char* pm_version(void) { return "pm_sample 0.2 sm_100a"; }
 

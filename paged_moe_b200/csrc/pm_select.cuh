@@ -105,7 +105,7 @@ __device__ uint64_t warp_select_topk(uint64_t* buf, int cnt, int K, unsigned* hi
 // Block-level: the K largest of U[0..n) sorted descending into S[0..m),
 // m = min(n, K), returned to every thread.  U may be clobbered.  hist is a
 // 256-word shared array, scal 4 shared ints.  Call with all threads.
-__device__ int block_topk_sorted(uint64_t* U, int n, int K, uint64_t* S, int S_cap, unsigned* hist,
+__device__ inline int block_topk_sorted(uint64_t* U, int n, int K, uint64_t* S, int S_cap, unsigned* hist,
                                  int* scal) {
   const int tid = threadIdx.x, nth = blockDim.x;
   int m;

@@ -253,7 +253,7 @@ __device__ __forceinline__ uint64_t row_u53(const SampleArgs& a, int64_t row, in
 // Returns the token, or -1 when the survivors reach past the candidates (the
 // row is then flagged; only possible when top_k is off).  *n_out = survivors;
 // *x_out (when given) = the token's value, S's value at its rank.
-__device__ int warp_filter_draw(const SampleArgs& a, const pm_row_params& p, int64_t row, const uint64_t* S,
+__device__ inline int warp_filter_draw(const SampleArgs& a, const pm_row_params& p, int64_t row, const uint64_t* S,
                                 int m, bool complete, float c, int* n_out, const float* scores = nullptr,
                                 float* x_out = nullptr) {
   const int lane = threadIdx.x & 31;
@@ -323,7 +323,7 @@ __device__ int warp_filter_draw(const SampleArgs& a, const pm_row_params& p, int
 
 // Renormalised survivor probabilities at temperature (fp64, rank order,
 // sequential sum) into the row's output slots.  Lane 0.
-__device__ __noinline__ void write_survivors(const SampleArgs& a, const pm_row_params& p, int64_t row,
+__device__ inline __noinline__ void write_survivors(const SampleArgs& a, const pm_row_params& p, int64_t row,
                                                 const uint64_t* S, int cnt) {
   double ymax = -INFINITY;
   for (int r = 0; r < cnt; ++r) {
@@ -579,6 +579,45 @@ __device__ __noinline__ int warp_row_merge(const SampleArgs& a, int64_t row, int
     tok = warp_full_draw<T>(a, p, row, x_tok);
   }
   return tok;
+}
+
+// Row outputs (lane 0).
+__device__ __forceinline__ void write_row(const SampleArgs& a, int64_t row, int mode, int tok, float x_tok,
+                                          float lse, int ns) {
+  const int32_t prevs = a.status_live ? ld_cg(&a.status[row]) : 0;
+  a.status[row] = prevs | (tok < 0 ? 1 : 0);
+  a.tokens[row] = tok;
+  if (a.lse_out) a.lse_out[row] = lse;
+  if (a.row_lse) a.row_lse[row] = lse;
+  if (a.tok_logprob) a.tok_logprob[row] = tok >= 0 ? fsub(x_tok, lse) : __int_as_float(0x7fc00000);
+  if (a.n_surv && (mode != kCand || !a.surv_ids)) a.n_surv[row] = mode == kCand ? ns : 0;
+}
+
+// The processed logit of one token of a row (bias, penalties, mask): the
+// single-token form of process_tile, for the rare paths.
+__device__ inline __noinline__ float processed_value(const SampleArgs& a, int dtype, const pm_row_params& p, int64_t row, int tok) {
+  float x;
+  if (dtype == PM_DTYPE_F32) x = reinterpret_cast<const float*>(a.logits)[row * a.row_stride + tok];
+  else x = bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(a.logits)[row * a.row_stride + tok]);
+  const int tile = tok / kTile;
+  if (a.bias_off)
+    for (int i = a.bias_off[tile]; i < a.bias_off[tile + 1]; ++i)
+      if (a.bias_tok[i] == tok) x = fadd(x, a.bias_val[i]);
+  if (a.ovr_off) {
+    const int32_t* off = a.ovr_off + row * (int64_t)(a.n_tiles + 1) + tile;
+    const int32_t* otok = a.ovr_tok + row * (int64_t)a.ovr_cap;
+    int lo = off[0];
+    while (lo < off[1] && otok[lo] != tok) ++lo;  // a tile's entries are in no particular order
+    if (lo < off[1]) {
+      const uint32_t info = a.ovr_info[row * (int64_t)a.ovr_cap + lo];
+      if (info & 1u) x = x < 0.0f ? fmul(x, p.repetition_penalty) : __fdiv_rn(x, p.repetition_penalty);
+      if (info & 2u) x = fsub(x, p.presence_penalty);
+      const uint32_t cnt = info >> 8;
+      if (cnt) x = fsub(x, fmul(p.frequency_penalty, (float)cnt));
+    }
+  }
+  if (a.mask && !((a.mask[row * a.mask_stride + (tok >> 5)] >> (tok & 31)) & 1u)) x = -INFINITY;
+  return x;
 }
 
 }  // namespace pm
