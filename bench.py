@@ -50,8 +50,12 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--c5-rows", type=int, default=1024,
                     help="rows of the C5 workload (smaller only for profiling captures)")
-    ap.add_argument("--workload", default="c3", choices=["c3", "c5", "c1", "c2", "c2b", "c4a", "c4b"],
-                    help="c3 (default): the headline metric's config; c5: vocabulary-sharded sampling over the ranks")
+    ap.add_argument("--workload", default="c3",
+                    choices=["c3", "c5", "c5e", "c1", "c2", "c2b", "c4a", "c4b", "ngram", "think", "logprobs"],
+                    help="c3 (default): the headline metric's config; c5: C5 rows (one GPU: the unsharded pass; "
+                         "torchrun: vocabulary-sharded over the ranks); c5e: eight vocabulary shards emulated on "
+                         "one GPU; the rest: the other configs and the path's neighbours (n-gram drafts, "
+                         "ThinkBudget, log-softmax rows)")
     return ap.parse_args()
 
 
@@ -430,10 +434,15 @@ def run_c5(args):
         del x
     stream = torch.cuda.current_stream(dev)
 
+    import paged_moe_b200 as pm
+    emulated = args.workload == "c5e"
+
     def step(i):
         if world > 1:
             return S.sample_vocab_sharded(xs[i & 1], s, vocab_total=V, seed=3, offset=i)
-        return S.emulate(xs[i & 1], 1, s, seed=3, offset=i)
+        if emulated:
+            return S.emulate(xs[i & 1], 8, s, seed=3, offset=i)
+        return pm.sample_rows(xs[i & 1], s, seed=3, offset=i)
 
     for i in range(args.warmup):
         step(i)
@@ -467,15 +476,18 @@ def run_c5(args):
         "metric": "sampled rows/s, vocabulary-sharded C5", "value": B / (ms_step / 1000.0), "unit": "rows/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"C5: {B:,} rows, V=262,144 fp32 in {world} slices of {w} ids, temp 0.8, top_k 64, "
-                               "top_p 0.9; summarize + all-gather + merge per step",
+        "config": {"workload": (f"C5: {B:,} rows, V=262,144 fp32 in {world} slices of {w} ids, temp 0.8, top_k 64, "
+                                "top_p 0.9; summarize + all-gather + merge per step") if world > 1 else
+                               (f"C5: {B:,} rows, V=262,144 fp32, temp 0.8, top_k 64, top_p 0.9; " +
+                                ("eight vocabulary shards emulated on one GPU (summaries + merge)" if emulated else
+                                 "one unsharded pass (streaming + per-row merge)")),
                    "l2": "two alternating input batches larger than L2 per rank" if B * w * 4 > 126e6 else
                          "two alternating input batches"},
         "p50_us_per_step": 1000 * statistics.median(per),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None, "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs",
                      "algorithmic_bytes_per_launch": bytes_gpu},
-        "gpu_launches": 3 * args.steps,  # k_sample_stream, k_shard_pack, k_shard_merge
+        "gpu_launches": (3 if world > 1 else (17 if emulated else 2)) * args.steps,
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -495,7 +507,7 @@ def run_config(args):
     wl = args.workload
     # batches in rotation: enough that one pass over them exceeds the 126 MB
     # L2 twice (C1's 0.6 MB row is latency-bound and stays L2-resident)
-    nb = {"c1": 2, "c2": 16, "c2b": 16, "c4a": 4, "c4b": 4}[wl]
+    nb = {"c1": 2, "c2": 16, "c2b": 16, "c4a": 4, "c4b": 4, "ngram": 2, "think": 2, "logprobs": 6}[wl]
     if wl == "c1":
         ds = [W.c1(seed=k) for k in range(nb)]
         xs = [torch.from_numpy(d["logits"]).to(dev) for d in ds]
@@ -517,6 +529,35 @@ def run_config(args):
             return pm.sample_rows(xs[i % nb], s, p, history=hs[i % nb], seed=5, offset=i)
         desc = ("C2: B=64, V=151,936 bf16, 4,096-id Zipf histories, presence 0.5 + frequency 0.3, "
                 + ("min_p 0.05 at temp 1" if wl == "c2b" else "argmax"))
+    elif wl == "ngram":
+        from paged_moe_b200 import ngram
+        hs = [torch.from_numpy(W.ngram_histories(seed=k)).to(dev) for k in range(nb)]
+        rows, nbytes = 32, 32 * 4096 * 4
+
+        def step(i):
+            return ngram.draft_ngram_batch(hs[i % nb], 4)
+        desc = "n-gram drafts: 32 requests x 4,096-token histories (repeated spans), k=4, n 8..3"
+    elif wl == "think":
+        from paged_moe_b200.think_budget import ThinkBudget
+        tb = ThinkBudget(W.SyntheticTokenizer(), chars=6000, close="", device=dev, slack=48)
+        gens = [torch.from_numpy(np.random.default_rng(k).integers(0, 151935, (256, 2048)).astype(np.int32)).to(dev)
+                for k in range(nb)]
+        rows, nbytes = 256, 256 * 2048 * 4
+
+        def step(i):
+            return tb.forced(gens[i % nb])
+        desc = "ThinkBudget: 256 rows x 2,048 generated ids, vocabulary 151,936, budget 6,000 characters"
+    elif wl == "logprobs":
+        ds = [W.c1(seed=k, B=64) for k in range(nb)]
+        xs = [torch.from_numpy(d["logits"]).to(dev) for d in ds]
+        hs = [torch.from_numpy(d["hist"]).to(dev) for d in ds]
+        p = ds[0]["proc"]
+        rows, nbytes = 64, 64 * 151936 * 8
+        outs = [torch.empty(64, 151936, dtype=torch.float32, device=dev) for _ in range(2)]
+
+        def step(i):
+            return pm.logprobs(xs[i % nb], p, history=hs[i % nb], out=outs[i & 1])
+        desc = "log-softmax rows: B=64, V=151,936 fp32, repetition penalty 1.05 over 256 ids (read V, write V)"
     else:
         ds = [W.c4(seed=k) for k in range(nb)]
         tg = [torch.from_numpy(d["target"]).to(dev) for d in ds]
@@ -589,7 +630,7 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload == "c5":
+    elif args.workload in ("c5", "c5e"):
         run_c5(args)
     elif args.workload != "c3":
         run_config(args)

@@ -129,3 +129,48 @@ def c5(seed: int = 0, B: int = 1024, V: int = 262144):
     x = peaked_logits(rng, B, V, 2.5, 10.0, 32)
     s = SamplerSettings(temp=0.8, top_k=64, top_p=0.9)
     return dict(logits=x, sampler=s, proc=ProcessorSettings())
+
+
+class SyntheticTokenizer:
+    """A tokenizer stand-in for the ThinkBudget workload: vocabulary `V`,
+    piece i decodes to a seeded string of 1..8 characters, every 17th piece
+    ends a sentence, and the think end tag is the last id."""
+
+    def __init__(self, V: int = 151936, seed: int = 0):
+        rng = np.random.default_rng(seed)
+        self.V = V
+        self.think_end_id = V - 1
+        self._lens = rng.integers(1, 9, V)
+
+    def get_vocab(self):
+        return {f"t{i}": i for i in range(self.V)}
+
+    def batch_decode(self, ids):
+        out = []
+        for (i,) in ids:
+            if i == self.think_end_id:
+                out.append("</think>")
+            else:
+                out.append("x" * (int(self._lens[i]) - 1) + ("." if i % 17 == 0 else "a"))
+        return out
+
+    def encode(self, text, add_special_tokens=False):
+        return [11, 12, 13, self.think_end_id]
+
+
+def ngram_histories(seed: int = 0, B: int = 32, H: int = 4096, V: int = 151936):
+    """[B, H] histories made of repeated spans (so n-gram matches exist):
+    each row draws 64-token spans, a third of them copies of earlier spans."""
+    rng = np.random.default_rng(seed)
+    h = np.empty((B, H), dtype=np.int32)
+    for b in range(B):
+        pos = 0
+        while pos < H:
+            n = min(64, H - pos)
+            if pos >= 64 and rng.random() < 1 / 3:
+                src = int(rng.integers(0, pos - n + 1))
+                h[b, pos:pos + n] = h[b, src:src + n]
+            else:
+                h[b, pos:pos + n] = rng.integers(0, V, n)
+            pos += n
+    return h
