@@ -148,6 +148,26 @@ def load(build_if_missing: bool = True):
     return lib
 
 
+_ext = None
+
+
+def ext():
+    """The PyTorch extension module over the C ABI (_pm_torch), built first
+    when it is missing or older than its sources and a compiler exists."""
+    global _ext
+    if _ext is not None:
+        return _ext
+    load()
+    try:
+        _build.build_ext()
+    except Exception as e:  # no compiler here: the prebuilt module must exist
+        if not os.path.exists(_build.ext_path()):
+            raise ImportError(f"the _pm_torch extension is missing and could not be built: {e}") from e
+    from . import _pm_torch  # noqa: E402  (in-tree module next to libpm_sample.so)
+    _ext = _pm_torch
+    return _ext
+
+
 def check(rc: int, what: str) -> None:
     if rc == PM_OK:
         return

@@ -86,6 +86,46 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return SO
 
 
+EXT_SRC = os.path.join(CSRC, "pm_torch.cpp")
+
+
+def ext_path() -> str:
+    import sysconfig
+    return os.path.join(HERE, "_pm_torch" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_ext(force: bool = False, verbose: bool = False) -> str:
+    """Compile the PyTorch extension module _pm_torch (pm_torch.cpp) against
+    torch's headers, linked to libpm_sample.so beside it (rpath $ORIGIN)."""
+    import sysconfig
+    out = ext_path()
+    deps = [EXT_SRC, os.path.join(ROOT, "include", "pm_sample.h"), SO]
+    if not force and os.path.exists(out) and all(os.path.getmtime(d) <= os.path.getmtime(out) for d in deps):
+        return out
+    import torch
+    from torch.utils import cpp_extension as ce
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_pm_torch", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           f"-I{sysconfig.get_paths()['include']}", f"-I{os.path.join(cuda_home, 'include')}"]
+    cmd += [f"-I{p}" for p in ce.include_paths()]
+    cmd += ["-o", out + ".tmp", EXT_SRC]
+    cmd += [f"-L{p}" for p in ce.library_paths()]
+    cmd += [f"-L{HERE}", "-lpm_sample", "-Wl,-rpath,$ORIGIN",
+            "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
+            f"-L{os.path.join(cuda_home, 'lib64')}", "-lcudart"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError("building the _pm_torch extension failed")
+    os.replace(out + ".tmp", out)
+    return out
+
+
 if __name__ == "__main__":
     build(force="--force" in sys.argv, verbose=True)
     print(SO)
+    print(build_ext(force="--force" in sys.argv, verbose=True))

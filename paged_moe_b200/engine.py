@@ -109,64 +109,129 @@ def _params_for(dev: torch.device, sampler, processors, B: int, V: int):
     return hit
 
 
-def build_rows(logits: torch.Tensor, sampler, processors, history, history_len, mask, keep: _Keep,
-               feed: Optional[torch.Tensor] = None, feed_group: int = 0,
-               forced: Optional[torch.Tensor] = None) -> L.Rows:
+def device_of(logits: torch.Tensor) -> torch.device:
+    """The CUDA device a call on these logits runs on (the current one for
+    host logits)."""
+    return logits.device if logits.is_cuda else torch.device("cuda", torch.cuda.current_device())
+
+
+def _gather_reads_host(logits: torch.Tensor, mask) -> bool:
+    """Whether the masked gather pass can read these host logits in place:
+    pinned (so the device reaches them at the same address), a mask given,
+    and values the pass fetches as aligned 4-byte words (fp32, or bf16 rows of
+    even stride)."""
+    if logits.is_cuda or mask is None or not logits.is_pinned():
+        return False
+    if mask.is_cuda is False and not mask.is_pinned():
+        return False
+    if logits.dtype == torch.float32:
+        return True
+    return logits.dtype == torch.bfloat16 and logits.stride(0) % 2 == 0 and logits.data_ptr() % 4 == 0
+
+
+class Prepared:
+    """The tensors of one call, ready for the C ABI: every one on the call's
+    device (host logits and mask only when the masked pass reads them in
+    place), contiguous, int32 ids."""
+
+    __slots__ = ("dev", "logits", "params", "flags_any", "top_k_max", "per_row", "procs", "hist", "hist_len",
+                 "feed", "feed_group", "bias_tok", "bias_val", "mask", "forced")
+
+
+def prepare(logits: torch.Tensor, sampler, processors, history, history_len, mask, keep: _Keep,
+            feed: Optional[torch.Tensor] = None, feed_group: int = 0,
+            forced: Optional[torch.Tensor] = None, allow_host: bool = False) -> Prepared:
+    """Logits on a CUDA device are used in place.  With allow_host, pinned
+    host logits with a mask stay in host memory when the masked gather pass
+    takes them: it reads the mask and the allowed logits over the host link,
+    nothing else; other host logits are copied to the device first."""
     if logits.dim() != 2:
         raise ValueError("logits must be [rows, vocab]")
+    dev = device_of(logits)
     if not logits.is_cuda:
-        raise ValueError("logits must be a CUDA tensor")
+        if not logits.is_pinned():
+            raise ValueError("logits must be a CUDA tensor or pinned host memory")
+        if not (allow_host and logits.stride(1) == 1 and _gather_reads_host(logits, mask)):
+            logits = keep(logits.to(dev, non_blocking=True))
     if logits.stride(1) != 1:
         logits = keep(logits.contiguous())
+    _dtype_code(logits)
     B, V = logits.shape
-    dev = logits.device
-    params, flags_any, top_k_max, per_row, procs, bias = _params_for(dev, sampler, processors, B, V)
-    r = L.Rows()
-    r.logits = logits.data_ptr()
-    r.dtype = _dtype_code(logits)
-    r.rows = B
-    r.vocab = V
-    r.row_stride = logits.stride(0)
-    r.params = params.data_ptr()
-    r.params_per_row = 1 if per_row else 0
-    r.flags_any = flags_any
-    r.top_k_max = top_k_max
-    if history is not None and any(p.penalties_on for p in procs):
+    q = Prepared()
+    q.dev = dev
+    q.logits = keep(logits)
+    q.params, q.flags_any, q.top_k_max, q.per_row, q.procs, bias = _params_for(dev, sampler, processors, B, V)
+    q.hist = q.hist_len = q.feed = q.bias_tok = q.bias_val = q.mask = q.forced = None
+    q.feed_group = 0
+    if history is not None and any(p.penalties_on for p in q.procs):
         h = history
         if h.dim() == 1:
             h = h.unsqueeze(0).expand(B if feed is None else B // feed_group, -1)
-        h = keep(h.to(device=dev, dtype=torch.int32).contiguous())
-        r.hist = h.data_ptr()
-        r.hist_stride = h.shape[1]
+        q.hist = keep(h.to(device=dev, dtype=torch.int32).contiguous())
         if history_len is not None:
-            hl = keep(torch.as_tensor(history_len, dtype=torch.int32, device=dev).contiguous())
-            r.hist_len = hl.data_ptr()
+            q.hist_len = keep(torch.as_tensor(history_len, dtype=torch.int32, device=dev).contiguous())
     if feed is not None:
-        f = keep(feed.to(device=dev, dtype=torch.int32).contiguous())
-        r.feed = f.data_ptr()
-        r.feed_group = feed_group
-        if not r.hist:
+        q.feed = keep(feed.to(device=dev, dtype=torch.int32).contiguous())
+        q.feed_group = feed_group
+        if q.hist is None:
             # the feed alone is the history
-            dummy = keep(torch.zeros((B // feed_group, 1), dtype=torch.int32, device=dev))
-            hl = keep(torch.zeros(B // feed_group, dtype=torch.int32, device=dev))
-            r.hist, r.hist_len, r.hist_stride = dummy.data_ptr(), hl.data_ptr(), 1
+            q.hist = keep(torch.zeros((B // feed_group, 1), dtype=torch.int32, device=dev))
+            q.hist_len = keep(torch.zeros(B // feed_group, dtype=torch.int32, device=dev))
     if bias is not None:
-        r.bias_tokens, r.bias_values, r.n_bias = bias[0].data_ptr(), bias[1].data_ptr(), bias[2]
+        q.bias_tok, q.bias_val = bias[0], bias[1]
     if mask is not None:
         m = mask
         if m.dtype not in (torch.int32, torch.uint32):
             raise TypeError("mask must be packed 32-bit words (int32 or uint32)")
         if m.dim() == 1:
             m = m.unsqueeze(0).expand(B, -1)
-        m = keep(m.to(dev).contiguous())
+        if m.is_cuda or logits.is_cuda:
+            m = keep(m.to(dev, non_blocking=True).contiguous())
+        else:  # host logits read in place: the mask too
+            m = keep(m if m.is_contiguous() else m.contiguous().pin_memory())
         if m.shape[1] < (V + 31) // 32:
             raise ValueError("mask has fewer than ceil(vocab/32) words per row")
-        r.mask = m.data_ptr()
-        r.mask_stride = m.shape[1]
+        q.mask = m
     if forced is not None:
-        f = keep(torch.as_tensor(forced, device=dev).to(torch.int32).reshape(B).contiguous())
-        r.forced = f.data_ptr()
-    keep(logits)
+        q.forced = keep(torch.as_tensor(forced, device=dev).to(torch.int32).reshape(B).contiguous())
+    return q
+
+
+def _i64(v: int) -> int:
+    """A 64-bit unsigned value as the signed int64 with the same bits."""
+    v &= 0xFFFFFFFFFFFFFFFF
+    return v - (1 << 64) if v >= (1 << 63) else v
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def build_rows(logits: torch.Tensor, sampler, processors, history, history_len, mask, keep: _Keep,
+               feed: Optional[torch.Tensor] = None, feed_group: int = 0,
+               forced: Optional[torch.Tensor] = None, allow_host: bool = False) -> L.Rows:
+    """The pm_rows struct (ctypes) for a call; see prepare()."""
+    q = prepare(logits, sampler, processors, history, history_len, mask, keep, feed, feed_group, forced, allow_host)
+    B, V = q.logits.shape
+    r = L.Rows()
+    r.logits = q.logits.data_ptr()
+    r.dtype = _dtype_code(q.logits)
+    r.rows = B
+    r.vocab = V
+    r.row_stride = q.logits.stride(0)
+    r.params = q.params.data_ptr()
+    r.params_per_row = 1 if q.per_row else 0
+    r.flags_any = q.flags_any
+    r.top_k_max = q.top_k_max
+    if q.hist is not None:
+        r.hist, r.hist_stride, r.hist_len = q.hist.data_ptr(), q.hist.shape[1], _ptr(q.hist_len)
+    if q.feed is not None:
+        r.feed, r.feed_group = q.feed.data_ptr(), q.feed_group
+    if q.bias_tok is not None:
+        r.bias_tokens, r.bias_values, r.n_bias = q.bias_tok.data_ptr(), q.bias_val.data_ptr(), q.bias_tok.numel()
+    if q.mask is not None:
+        r.mask, r.mask_stride = q.mask.data_ptr(), q.mask.shape[1]
+    r.forced = _ptr(q.forced)
     return r
 
 
@@ -197,6 +262,10 @@ def sample_rows(logits: torch.Tensor, sampler: Union[SamplerSettings, Sequence[S
                 forced: Optional[torch.Tensor] = None):
     """Processors + log-softmax + sampler for every row, one fused pass.
 
+    logits [B, V] on a CUDA device, or in pinned host memory: with a mask,
+    the masked pass then reads only the mask and the allowed logits from
+    host memory (no copy of the rows); without one they are copied first.
+
     Returns a dict with "tokens" [B] int32 (and "lse", "logprob",
     "surv_ids"/"surv_probs"/"n_surv" when asked), all on the logits' device,
     enqueued on the current stream.  "status" [B] is non-zero for a row whose
@@ -204,38 +273,30 @@ def sample_rows(logits: torch.Tensor, sampler: Union[SamplerSettings, Sequence[S
     restricts a row to one token (the ThinkBudget hook).
     """
     keep = _Keep()
-    lib = L.load()
-    dev = logits.device
-    r = build_rows(logits, sampler, processors, history, history_len, mask, keep, forced=forced)
-    B, V = r.rows, r.vocab
-    nz = _noise(B, V, seed, offset, row_base, gumbel, uniform, keep, dev)
-    out = L.SampleOut()
-    tokens = torch.empty(B, dtype=torch.int32, device=dev)
-    out.tokens = tokens.data_ptr()
-    res = {"tokens": tokens}
-    if return_lse:
-        res["lse"] = torch.empty(B, dtype=torch.float32, device=dev)
-        out.lse = res["lse"].data_ptr()
-    if return_logprob:
-        res["logprob"] = torch.empty(B, dtype=torch.float32, device=dev)
-        out.token_logprob = res["logprob"].data_ptr()
-    if survivors:
-        res["surv_ids"] = torch.empty((B, survivors), dtype=torch.int32, device=dev)
-        res["surv_probs"] = torch.empty((B, survivors), dtype=torch.float32, device=dev)
-        res["n_surv"] = torch.empty(B, dtype=torch.int32, device=dev)
-        out.surv_ids = res["surv_ids"].data_ptr()
-        out.surv_probs = res["surv_probs"].data_ptr()
-        out.n_surv = res["n_surv"].data_ptr()
-        out.surv_cap = survivors
-    nbytes = lib.pm_sample_workspace_bytes(C.byref(r))
+    E = L.ext()
+    q = prepare(logits, sampler, processors, history, history_len, mask, keep, forced=forced, allow_host=True)
+    dev = q.dev
+    g = u = None
+    if gumbel is not None:
+        g = keep(gumbel.to(device=dev, dtype=torch.float32).contiguous())
+    if uniform is not None:
+        u = keep(uniform.to(device=dev, dtype=torch.float64).contiguous())
+    nbytes = E.sample_workspace_bytes(q.logits, q.params, q.per_row, q.flags_any, q.top_k_max, q.hist, q.mask)
     if nbytes == 0:
         L.check(L.PM_ERR_UNSUPPORTED, "pm_sample_workspace_bytes")
-    stream = torch.cuda.current_stream(dev)
-    ws = workspace(nbytes, dev, stream)
-    rc = lib.pm_sample_rows(C.byref(r), C.byref(nz), C.byref(out), ws.data_ptr(), ws.numel(), stream.cuda_stream)
-    L.check(rc, "pm_sample_rows")
+    ws = workspace(nbytes, dev)
+    out = E.sample_rows(q.logits, q.params, q.per_row, q.flags_any, q.top_k_max, q.hist, q.hist_len, q.bias_tok,
+                        q.bias_val, q.mask, q.forced, _i64(seed), _i64(offset), row_base, g, u, return_lse,
+                        return_logprob, survivors, ws)
+    res = {"tokens": out[0]}
+    if return_lse:
+        res["lse"] = out[1]
+    if return_logprob:
+        res["logprob"] = out[2]
+    if survivors:
+        res["surv_ids"], res["surv_probs"], res["n_surv"] = out[3], out[4], out[5]
     if return_status:
-        res["status"] = status_view(ws, r)
+        res["status"] = ws[: 4 * q.logits.shape[0]].view(torch.int32).clone()
     return res
 
 
@@ -250,7 +311,7 @@ def apply_processors(logits: torch.Tensor, processors=None, history=None, histor
     return_status, (logits, per-row status [B] int32)."""
     keep = _Keep()
     lib = L.load()
-    dev = logits.device
+    dev = device_of(logits)
     r = build_rows(logits, SamplerSettings(), processors, history, history_len, mask, keep)
     if out is None:
         out = torch.empty((r.rows, r.vocab), dtype=torch.float32, device=dev)
@@ -272,7 +333,7 @@ def logprobs(logits: torch.Tensor, processors=None, history=None, history_len=No
     """(processed logits - row log-sum-exp, lse) in fp32."""
     keep = _Keep()
     lib = L.load()
-    dev = logits.device
+    dev = device_of(logits)
     r = build_rows(logits, SamplerSettings(), processors, history, history_len, mask, keep)
     if out is None:
         out = torch.empty((r.rows, r.vocab), dtype=torch.float32, device=dev)

@@ -106,6 +106,7 @@ class ThinkBudget:
         self.close = torch.tensor(self.close_ids, dtype=torch.int32, device=self.device)
         self.lens, self.ends = piece_tables(tokenizer, self.device)
         self.base: Optional[int] = None  # sequence length at the first call (the prompt's tail)
+        self._budgets: Dict[int, torch.Tensor] = {}
 
     def forced(self, gen: torch.Tensor, gen_len: Optional[torch.Tensor] = None,
                chars: Optional[Sequence[int]] = None) -> torch.Tensor:
@@ -116,8 +117,12 @@ class ThinkBudget:
         g = g.to(torch.int32).contiguous()
         B, T = g.shape
         gl = None if gen_len is None else torch.as_tensor(gen_len, device=self.device).to(torch.int32).contiguous()
-        ch = torch.tensor(list(chars) if chars is not None else [self.chars] * B, dtype=torch.int32,
-                          device=self.device)
+        if chars is not None:
+            ch = torch.tensor(list(chars), dtype=torch.int32, device=self.device)
+        else:  # one budget for every row: a cached device tensor (no host copy per call)
+            ch = self._budgets.get(B)
+            if ch is None:
+                ch = self._budgets[B] = torch.full((B,), self.chars, dtype=torch.int32, device=self.device)
         out = torch.empty(B, dtype=torch.int32, device=self.device)
         start = -1 if self.open_in_prompt else (self.start_id if self.start_id >= 0 else 0x7fffffff)
         rc = L.load().pm_think_budget(g.data_ptr() if g.numel() else None, None if gl is None else gl.data_ptr(), T,

@@ -15,13 +15,12 @@ and keeps the target distribution exact at any temperature.
 
 from __future__ import annotations
 
-import ctypes as C
 from typing import Optional
 
 import torch
 
 from . import _lib as L
-from .engine import _Keep, _noise, build_rows, workspace
+from .engine import _i64, _Keep, prepare, workspace
 
 _MODES = {"match": L.PM_VERIFY_MATCH, "residual": L.PM_VERIFY_RESIDUAL}
 
@@ -67,59 +66,53 @@ def verify(target_logits: torch.Tensor, drafts: torch.Tensor, y: torch.Tensor, s
     x = target_logits.reshape(B * K1, V)
     dev = x.device
     keep = _Keep()
-    drafts = keep(drafts.to(device=dev, dtype=torch.int32).contiguous())
-    y = torch.as_tensor(y).reshape(B).to(device=dev, dtype=torch.int32)
+    if drafts.device != dev or drafts.dtype != torch.int32 or not drafts.is_contiguous():
+        drafts = keep(drafts.to(device=dev, dtype=torch.int32).contiguous())
     procs = _per_row(processors, B, K1)
     # the feed (y, then the drafts) extends the history the penalties read;
     # without a penalty nothing reads it
     plist = procs if isinstance(procs, list) else [procs]
     pens = any(p is not None and p.penalties_on for p in plist)
-    feed = keep(torch.cat([y[:, None], drafts], dim=1).contiguous()) if pens else None
+    feed = None
+    if pens:
+        y = torch.as_tensor(y).reshape(B).to(device=dev, dtype=torch.int32)
+        feed = keep(torch.cat([y[:, None], drafts], dim=1).contiguous())
     if mask is not None and mask.dim() == 3:
         mask = mask.reshape(B * K1, -1)
-    r = build_rows(x, _per_row(sampler, B, K1), procs, history, history_len, mask, keep,
-                   feed=feed, feed_group=K1 if pens else 0)
-    nz = _noise(B * K1, V, seed, offset, row_base, gumbel, uniform, keep, dev)
-    va = L.VerifyArgs()
-    va.mode = _MODES[mode]
-    va.drafts = drafts.data_ptr()
-    va.n_draft = k
+    q = prepare(x, _per_row(sampler, B, K1), procs, history, history_len, mask, keep,
+                feed=feed, feed_group=K1 if pens else 0)
+    g = None if gumbel is None else keep(gumbel.to(device=dev, dtype=torch.float32).contiguous())
+    u = None if uniform is None else keep(uniform.to(device=dev, dtype=torch.float64).contiguous())
+    dl = None
     if mode == "residual" and k > 0:
         if draft_logits is None:
             raise ValueError("residual mode needs the draft logits")
         dl = draft_logits.reshape(B * k, V)
+        if dl.dtype not in (torch.float32, torch.bfloat16):
+            raise TypeError(f"draft_logits must be float32 or bfloat16, got {dl.dtype}")
         if dl.stride(1) != 1:
             dl = dl.contiguous()
         if dl.device != dev:
             raise ValueError("draft_logits must be on the target logits' device")
         keep(dl)
-        va.draft_logits = dl.data_ptr()
-        va.draft_dtype = L.PM_DTYPE_F32 if dl.dtype == torch.float32 else L.PM_DTYPE_BF16
-        if dl.dtype not in (torch.float32, torch.bfloat16):
-            raise TypeError(f"draft_logits must be float32 or bfloat16, got {dl.dtype}")
-        va.draft_row_stride = dl.stride(0)
+    ua = ur = None
     if u_accept is not None:
         ua = keep(torch.as_tensor(u_accept).to(device=dev, dtype=torch.float64).reshape(B, k).contiguous())
-        va.u_accept = ua.data_ptr()
     if u_residual is not None:
         ur = keep(torch.as_tensor(u_residual).to(device=dev, dtype=torch.float64).reshape(B).contiguous())
-        va.u_residual = ur.data_ptr()
-    tokens = torch.empty((B, K1), dtype=torch.int32, device=dev)
-    nacc = torch.empty(B, dtype=torch.int32, device=dev)
-    va.tokens = tokens.data_ptr()
-    va.n_accepted = nacc.data_ptr()
-    res = {"tokens": tokens, "n_accepted": nacc}
-    if return_row_tokens:
-        res["row_tokens"] = torch.empty((B, K1), dtype=torch.int32, device=dev)
-        va.row_tokens = res["row_tokens"].data_ptr()
-    lib = L.load()
-    nbytes = lib.pm_verify_workspace_bytes(C.byref(r), C.byref(va))
+    E = L.ext()
+    m = _MODES[mode]
+    nbytes = E.verify_workspace_bytes(q.logits, q.params, q.per_row, q.flags_any, q.top_k_max, q.hist, q.feed,
+                                      q.feed_group, q.mask, m, drafts)
     if nbytes == 0:
         L.check(L.PM_ERR_UNSUPPORTED, "pm_verify_workspace_bytes")
-    stream = torch.cuda.current_stream(dev)
-    ws = workspace(nbytes, dev, stream)
-    rc = lib.pm_verify(C.byref(r), C.byref(nz), C.byref(va), ws.data_ptr(), ws.numel(), stream.cuda_stream)
-    L.check(rc, "pm_verify")
+    ws = workspace(nbytes, dev)
+    out = E.verify(q.logits, q.params, q.per_row, q.flags_any, q.top_k_max, q.hist, q.hist_len, q.feed,
+                   q.feed_group, q.bias_tok, q.bias_val, q.mask, _i64(seed), _i64(offset), row_base, g, u, m, drafts,
+                   dl, ua, ur, return_row_tokens, ws)
+    res = {"tokens": out[0], "n_accepted": out[1]}
+    if return_row_tokens:
+        res["row_tokens"] = out[2]
     if return_status:
-        res["status"] = ws[: 4 * r.rows].view(torch.int32).clone()
+        res["status"] = ws[: 4 * B * K1].view(torch.int32).clone()
     return res

@@ -110,3 +110,29 @@ def test_c3_masked_philox_many_rows():
     d = W.c3(seed=21, B=40)
     ref, got = run_both(d["logits"], d["sampler"], mask=d["mask"], injected=False, surv=50)
     assert_same(ref, got, surv=50)
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_pinned_host_logits_read_in_place(bf16):
+    """Logits and mask left in pinned host memory: the masked pass reads only
+    the mask and the allowed logits from there; results equal the device run."""
+    from paged_moe_b200 import engine
+    rng = np.random.default_rng(41)
+    B, V = 12, 163840
+    x = W.peaked_logits(rng, B, V, 2.0, 9.0, 64)
+    mask = W.bitmask(rng, B, V)
+    s = SamplerSettings(temp=1.0, top_k=50, top_p=0.95)
+    if bf16:
+        xt = torch.from_numpy(W.to_bf16_bits(x).view(np.int16)).view(torch.bfloat16)
+    else:
+        xt = torch.from_numpy(x)
+    mt = torch.from_numpy(mask.view(np.int32))
+    kw = dict(seed=9, offset=4, return_lse=True, survivors=8, return_status=True)
+    dev = engine.sample_rows(xt.cuda(), s, mask=mt.cuda(), **kw)
+    host = engine.sample_rows(xt.pin_memory(), s, mask=mt.pin_memory(), **kw)
+    torch.cuda.synchronize()
+    assert host["tokens"].is_cuda
+    for k in ("tokens", "lse", "surv_ids", "n_surv", "status"):
+        assert torch.equal(host[k], dev[k]), k
+    ref = O.sample(O.bf16_to_f32(W.to_bf16_bits(x)) if bf16 else x, _osamp(s), mask=mask, seed=9, offset=4)
+    np.testing.assert_array_equal(host["tokens"].cpu().numpy(), ref["tokens"])
