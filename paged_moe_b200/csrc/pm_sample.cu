@@ -774,9 +774,11 @@ __global__ void __launch_bounds__(kThreadsS, kStreamBlocks<KC>) k_sample_stream(
 // --------------------------------------------------------------------------
 // processors / logprobs: per-tile stats pass and a write pass
 // --------------------------------------------------------------------------
+// out (when given) receives the processed logits, minus the row's
+// log-sum-exp sub[row] when sub is given (the log-softmax write pass).
 template <typename T>
 __global__ void __launch_bounds__(kThreadsS) k_process_rows(const __grid_constant__ SampleArgs a, float* out,
-                                                            int64_t out_stride, bool want_stats) {
+                                                            int64_t out_stride, bool want_stats, const float* sub) {
   constexpr int VW = Lay<T>::VW;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* wbuf = reinterpret_cast<float*>(smem_raw) + (threadIdx.x >> 5) * kTile;
@@ -800,10 +802,11 @@ __global__ void __launch_bounds__(kThreadsS) k_process_rows(const __grid_constan
     }
     if (out) {
       float* orow = out + row * out_stride + start;
+      const float c = sub ? sub[row] : 0.0f;
 #pragma unroll
       for (int s = 0; s < 32; ++s) {
         const int e = slot_elem<VW>(s, lane);
-        if (e < n_valid) orow[e] = ti.v[s];
+        if (e < n_valid) orow[e] = sub ? fsub(ti.v[s], c) : ti.v[s];
       }
     }
   }
@@ -816,16 +819,6 @@ __global__ void __launch_bounds__(kThreadsS) k_row_lse(const __grid_constant__ S
     float m;
     const float c = warp_combine(a.statx + row * a.n_tiles, a.n_tiles, &m);
     if ((threadIdx.x & 31) == 0) { if (lse_out) lse_out[row] = c; a.row_lse[row] = c; }
-  }
-}
-
-// out[r, :] -= lse[r]   (log-softmax write pass)
-__global__ void k_sub_lse(float* out, int64_t out_stride, int64_t rows, int64_t vocab, const float* lse) {
-  const int64_t n = rows * vocab;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / vocab, v = i % vocab;
-    float* p = out + r * out_stride + v;
-    *p = fsub(*p, lse[r]);
   }
 }
 
@@ -1266,7 +1259,8 @@ int launch_draft_lse(const pm_rows* rows, const pm_verify_args* v, const VLayout
   const int64_t work = V.D * (int64_t)V.L.n_tiles;
   int64_t grid = (work + pm::kWarpsS - 1) / pm::kWarpsS;
   if (grid > (int64_t)num_sms() * 16) grid = (int64_t)num_sms() * 16;
-  pm::k_process_rows<TD><<<(unsigned)grid, pm::kThreadsS, pm::kWarpsS * pm::kTile * 4, st>>>(da, nullptr, 0, true);
+  pm::k_process_rows<TD><<<(unsigned)grid, pm::kThreadsS, pm::kWarpsS * pm::kTile * 4, st>>>(da, nullptr, 0, true,
+                                                                                          nullptr);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   int64_t g2 = (V.D + pm::kWarpsS - 1) / pm::kWarpsS;
@@ -1355,11 +1349,16 @@ static int process_common(const pm_rows* rows, float* out, int64_t out_stride, f
   int64_t grid = (work + pm::kWarpsS - 1) / pm::kWarpsS;
   const int64_t cap = (int64_t)num_sms() * 16;
   if (grid > cap) grid = cap;
-  if (rows->dtype == PM_DTYPE_BF16)
-    pm::k_process_rows<__nv_bfloat16><<<(unsigned)grid, pm::kThreadsS, smem, st>>>(a, out, out_stride, logprobs);
-  else
-    pm::k_process_rows<float><<<(unsigned)grid, pm::kThreadsS, smem, st>>>(a, out, out_stride, logprobs);
-  cudaError_t e = cudaGetLastError();
+  // processors: one pass writing the processed rows.  log-softmax: a pass
+  // for the tile statistics only (nothing written), the row log-sum-exp,
+  // then one pass writing processed - log-sum-exp.
+  const bool bf = rows->dtype == PM_DTYPE_BF16;
+  auto pass = [&](float* o, bool stats, const float* sub) {
+    if (bf) pm::k_process_rows<__nv_bfloat16><<<(unsigned)grid, pm::kThreadsS, smem, st>>>(a, o, out_stride, stats, sub);
+    else pm::k_process_rows<float><<<(unsigned)grid, pm::kThreadsS, smem, st>>>(a, o, out_stride, stats, sub);
+    return cudaGetLastError();
+  };
+  cudaError_t e = logprobs ? pass(nullptr, true, nullptr) : pass(out, false, nullptr);
   if (e != cudaSuccess) return cuda_fail(e);
   if (logprobs) {
     int64_t g2 = (rows->rows + pm::kWarpsS - 1) / pm::kWarpsS;
@@ -1367,11 +1366,7 @@ static int process_common(const pm_rows* rows, float* out, int64_t out_stride, f
     pm::k_row_lse<<<(unsigned)g2, pm::kThreadsS, 0, st>>>(a, lse_out);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
-    const int64_t n = rows->rows * rows->vocab;
-    int64_t g3 = (n + 255) / 256;
-    if (g3 > (int64_t)num_sms() * 16) g3 = (int64_t)num_sms() * 16;
-    pm::k_sub_lse<<<(unsigned)g3, 256, 0, st>>>(out, out_stride, rows->rows, rows->vocab, a.row_lse);
-    e = cudaGetLastError();
+    e = pass(out, false, a.row_lse);
     if (e != cudaSuccess) return cuda_fail(e);
   }
   return PM_OK;

@@ -9,7 +9,10 @@
 
 namespace pm {
 
-constexpr uint32_t kWaitLimit = 1u << 24;  // polls of try_wait (each may suspend briefly)
+// Polls of try_wait; each may suspend the thread until the phase completes,
+// for at most kWaitHintNs: the whole wait is bounded by about 1.3 s.
+constexpr uint32_t kWaitLimit = 1u << 16;
+constexpr uint32_t kWaitHintNs = 20000;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -52,10 +55,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitHintNs)
       : "memory");
   return ok != 0;
 }
