@@ -143,24 +143,29 @@ def prepare(logits: torch.Tensor, sampler, processors, history, history_len, mas
             forced: Optional[torch.Tensor] = None, allow_host: bool = False) -> Prepared:
     """Logits on a CUDA device are used in place.  With allow_host, pinned
     host logits with a mask stay in host memory when the masked gather pass
-    takes them: it reads the mask and the allowed logits over the host link,
-    nothing else; other host logits are copied to the device first."""
+    takes them and no row has an unbounded filter: the pass reads the mask and
+    the allowed logits over the host link, nothing else; other host logits are
+    copied to the device first."""
     if logits.dim() != 2:
         raise ValueError("logits must be [rows, vocab]")
     dev = device_of(logits)
-    if not logits.is_cuda:
-        if not logits.is_pinned():
-            raise ValueError("logits must be a CUDA tensor or pinned host memory")
-        if not (allow_host and logits.stride(1) == 1 and _gather_reads_host(logits, mask)):
-            logits = keep(logits.to(dev, non_blocking=True))
-    if logits.stride(1) != 1:
-        logits = keep(logits.contiguous())
     _dtype_code(logits)
     B, V = logits.shape
     q = Prepared()
     q.dev = dev
-    q.logits = keep(logits)
     q.params, q.flags_any, q.top_k_max, q.per_row, q.procs, bias = _params_for(dev, sampler, processors, B, V)
+    if not logits.is_cuda:
+        if not logits.is_pinned():
+            raise ValueError("logits must be a CUDA tensor or pinned host memory")
+        # in place only when the gather pass is the one reader: rows with an
+        # unbounded filter may need the wide pass, which streams whole rows
+        in_place = (allow_host and logits.stride(1) == 1 and not (q.flags_any & L.PM_F_UNBOUNDED)
+                    and _gather_reads_host(logits, mask))
+        if not in_place:
+            logits = keep(logits.to(dev, non_blocking=True))
+    if logits.stride(1) != 1:
+        logits = keep(logits.contiguous())
+    q.logits = keep(logits)
     q.hist = q.hist_len = q.feed = q.bias_tok = q.bias_val = q.mask = q.forced = None
     q.feed_group = 0
     if history is not None and any(p.penalties_on for p in q.procs):

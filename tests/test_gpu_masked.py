@@ -136,3 +136,25 @@ def test_pinned_host_logits_read_in_place(bf16):
         assert torch.equal(host[k], dev[k]), k
     ref = O.sample(O.bf16_to_f32(W.to_bf16_bits(x)) if bf16 else x, _osamp(s), mask=mask, seed=9, offset=4)
     np.testing.assert_array_equal(host["tokens"].cpu().numpy(), ref["tokens"])
+
+
+def test_pinned_host_logits_unbounded_rows_copied():
+    """Rows with an unbounded filter (min_p, top_k off) may need the wide
+    pass over whole rows: pinned host logits are copied to the device first,
+    and the results equal the device run."""
+    from paged_moe_b200 import engine
+    rng = np.random.default_rng(43)
+    B, V = 6, 65536
+    x = W.peaked_logits(rng, B, V, 2.0, 9.0, 64)
+    mask = W.bitmask(rng, B, V)
+    s = SamplerSettings(temp=1.0, min_p=0.02)
+    xt = torch.from_numpy(x)
+    mt = torch.from_numpy(mask.view(np.int32))
+    kw = dict(seed=3, offset=1, return_lse=True, return_status=True)
+    dev = engine.sample_rows(xt.cuda(), s, mask=mt.cuda(), **kw)
+    host = engine.sample_rows(xt.pin_memory(), s, mask=mt.pin_memory(), **kw)
+    torch.cuda.synchronize()
+    for k in ("tokens", "lse", "status"):
+        assert torch.equal(host[k], dev[k]), k
+    ref = O.sample(x, _osamp(s), mask=mask, seed=3, offset=1)
+    np.testing.assert_array_equal(host["tokens"].cpu().numpy(), ref["tokens"])
