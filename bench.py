@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--c5-rows", type=int, default=1024,
                     help="rows of the C5 workload (smaller only for profiling captures)")
     ap.add_argument("--workload", default="c3",
-                    choices=["c3", "c5", "c5e", "c1", "c2", "c2b", "c4a", "c4b", "ngram", "think", "logprobs"],
+                    choices=["c3", "c3u", "c5", "c5e", "c1", "c2", "c2b", "c4a", "c4b", "ngram", "think", "logprobs"],
                     help="c3 (default): the headline metric's config; c5: C5 rows (one GPU: the unsharded pass; "
                          "torchrun: vocabulary-sharded over the ranks); c5e: eight vocabulary shards emulated on "
                          "one GPU; the rest: the other configs and the path's neighbours (n-gram drafts, "
@@ -504,7 +504,8 @@ def run_c5(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None, "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs",
                      "algorithmic_bytes_per_launch": bytes_gpu},
-        "gpu_launches": (3 if world > 1 else (17 if emulated else 2)) * args.steps,
+        # one GPU: streaming pass, row merge, exact pass for undecided top-p cuts
+        "gpu_launches": (3 if world > 1 else (17 if emulated else 3)) * args.steps,
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -524,8 +525,24 @@ def run_config(args):
     wl = args.workload
     # batches in rotation: enough that one pass over them exceeds the 126 MB
     # L2 twice (C1's 0.6 MB row is latency-bound and stays L2-resident)
-    nb = {"c1": 2, "c2": 16, "c2b": 16, "c4a": 4, "c4b": 4, "ngram": 2, "think": 2, "logprobs": 6}[wl]
-    if wl == "c1":
+    nb = {"c1": 2, "c2": 16, "c2b": 16, "c3u": 3, "c4a": 4, "c4b": 4, "ngram": 2, "think": 2, "logprobs": 6}[wl]
+    if wl == "c3u":
+        # C3's rows and filters without the mask: the dense filtered pass
+        gen = torch.Generator(device=dev)
+        xs = []
+        for k in range(nb):
+            gen.manual_seed(300 + k)
+            x = torch.randn(256, 163840, device=dev, generator=gen) * 2.0
+            idx = torch.randint(0, 163840, (256, 64), device=dev, generator=gen)
+            x.scatter_add_(1, idx, torch.full((256, 64), 9.0, device=dev))
+            xs.append(x)
+        s = SamplerSettings(temp=1.0, top_k=50, top_p=0.95)
+        rows, nbytes = 256, 256 * 163840 * 4
+
+        def step(i):
+            return pm.sample_rows(xs[i % nb], s, seed=5, offset=i)
+        desc = "C3 rows without the mask: B=256, V=163,840 fp32, temp 1.0, top_k 50, top_p 0.95 (dense filtered pass)"
+    elif wl == "c1":
         ds = [W.c1(seed=k) for k in range(nb)]
         xs = [torch.from_numpy(d["logits"]).to(dev) for d in ds]
         hs = [torch.from_numpy(d["hist"]).to(dev) for d in ds]

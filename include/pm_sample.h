@@ -266,6 +266,14 @@ PM_API int pm_think_budget(const int32_t *gen, const int32_t *gen_len, int64_t g
 PM_API int pm_sample_rows_static(const pm_rows *rows, const pm_noise *noise, const pm_sample_out *out,
                                  void *stream);
 
+/* Self-check of the hardware 2^a that the bracketed statistics rely on (no
+ * counterpart in the reference): evaluates it on the current device for
+ * every fp32 a in [-126, 1] and writes the largest relative error against
+ * the fp64 2^a to *max_rel_err (host memory).  Synchronous; allocates and
+ * frees a few bytes of device memory.  The library's error budget assumes
+ * at most 2^-20. */
+PM_API int pm_selfcheck_ex2(double *max_rel_err);
+
 /* Last CUDA error seen by this thread (cudaError_t value), 0 if none. */
 PM_API int pm_last_cuda_error(void);
 

@@ -103,6 +103,7 @@ class ShardArgs(C.Structure):
 _P = C.c_void_p
 SIGNATURES = {
     "pm_version": (C.c_char_p, []),
+    "pm_selfcheck_ex2": (C.c_int, [C.POINTER(C.c_double)]),
     "pm_last_cuda_error": (C.c_int, []),
     "pm_sample_workspace_bytes": (C.c_size_t, [_P]),
     "pm_sample_rows": (C.c_int, [_P, _P, _P, _P, C.c_size_t, _P]),
@@ -132,7 +133,7 @@ def load(build_if_missing: bool = True):
     if build_if_missing:
         try:
             path = _build.build()
-        except Exception as e:  # no nvcc on this machine: the prebuilt file must exist
+        except _build.CompilerMissing as e:  # no nvcc on this machine: the prebuilt file must exist
             if not os.path.exists(path):
                 raise ImportError(f"libpm_sample.so is missing and could not be built: {e}") from e
     if not os.path.exists(path):
@@ -160,7 +161,7 @@ def ext():
     load()
     try:
         _build.build_ext()
-    except Exception as e:  # no compiler here: the prebuilt module must exist
+    except _build.CompilerMissing as e:  # no compiler here: the prebuilt module must exist
         if not os.path.exists(_build.ext_path()):
             raise ImportError(f"the _pm_torch extension is missing and could not be built: {e}") from e
     from . import _pm_torch  # noqa: E402  (in-tree module next to libpm_sample.so)

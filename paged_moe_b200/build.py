@@ -27,11 +27,17 @@ NVCC_FLAGS = [
 ]
 
 
+class CompilerMissing(RuntimeError):
+    """No compiler on this machine: a prebuilt library is used as it is.
+    Any other build failure is an error (never a silent fall back to a stale
+    library)."""
+
+
 def nvcc() -> str:
     for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
         if cand and os.path.exists(cand):
             return cand
-    raise RuntimeError("nvcc not found")
+    raise CompilerMissing("nvcc not found")
 
 
 def sources() -> list:
@@ -102,11 +108,14 @@ def build_ext(force: bool = False, verbose: bool = False) -> str:
     deps = [EXT_SRC, os.path.join(ROOT, "include", "pm_sample.h"), SO]
     if not force and os.path.exists(out) and all(os.path.getmtime(d) <= os.path.getmtime(out) for d in deps):
         return out
+    cxx = os.environ.get("CXX", "g++")
+    if not shutil.which(cxx):
+        raise CompilerMissing(f"{cxx} not found")
     import torch
     from torch.utils import cpp_extension as ce
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
     cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
-    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden",
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden",
            f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_pm_torch", "-DTORCH_API_INCLUDE_EXTENSION_H",
            f"-I{sysconfig.get_paths()['include']}", f"-I{os.path.join(cuda_home, 'include')}"]
     cmd += [f"-I{p}" for p in ce.include_paths()]

@@ -102,6 +102,21 @@ __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
   return d;
 }
 
+__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+// fl32(log2 e): the multiplier of every base-2 exponent argument here.
+constexpr float kLog2eF = 0x1.715476p+0f;
+
+// The hardware 2^a (MUFU ex2, flush-to-zero).  Its bits are not specified,
+// so it serves only the bracketed statistics, whose error budget covers it
+// (relative error 2^-20; the GPU tests measure it).
+__device__ __forceinline__ float ex2_approx(float a) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+
 // q52 of two values at once; bit-identical to two q52 calls.
 __device__ __forceinline__ void q52x2(float d0, float d1, uint64_t& q0, uint64_t& q1) {
   const uint64_t D = pk(fmaxf(d0, -38.0f), fmaxf(d1, -38.0f));

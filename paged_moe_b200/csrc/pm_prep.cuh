@@ -35,6 +35,7 @@ struct PrepArgs {
   int32_t* ovr_off;   // [rows, n_tiles + 1]
   int32_t* status;    // [rows]
   uint64_t* row_tau;  // [rows] zeroed here for the streaming pass (or null)
+  int32_t* exact_q;   // [1 + rows]: the exact pass's queue count and tile counters, zeroed here (or null)
 };
 
 __device__ __forceinline__ int window_start(int H, int ctx) {
@@ -64,6 +65,10 @@ __global__ void __launch_bounds__(1024) k_prep_overrides(PrepArgs a) {
   asm volatile("griddepcontrol.launch_dependents;");
   if (r >= a.rows) return;
   if (a.row_tau && tid == 0) a.row_tau[r] = 0;
+  if (a.exact_q && tid == 0) {
+    a.exact_q[1 + r] = 0;
+    if (r == 0) a.exact_q[0] = 0;
+  }
   const pm_row_params p = a.params[a.params_per_row ? r : 0];
   const int64_t b = a.feed ? r / a.feed_group : r;
   const int fi = a.feed ? (int)(r % a.feed_group) : -1;

@@ -44,6 +44,7 @@ struct PartState {
   pm_row_params p;
   int mode;
   bool needx, needy;
+  bool needa;       // approximate statistics (the bracket) instead of needx
   int K;            // candidates kept per part
   float best_x;
   int best_e;
@@ -62,6 +63,7 @@ __device__ __forceinline__ void part_begin(const SampleArgs& a, int64_t row, int
   ps.p = row_params(a, row);
   ps.mode = row_mode(ps.p);
   ps.needx = needs_xstats(a, ps.p, ps.mode);
+  ps.needa = needs_astats(a, ps.p, ps.mode);
   ps.needy = ps.mode == kFullDraw;
   ps.K = (ps.p.top_k > 0 && ps.p.top_k < KC) ? ps.p.top_k : KC;
   ps.best_x = -INFINITY;          // a part whose values are all -inf answers its first token
@@ -425,6 +427,206 @@ __device__ __forceinline__ void scan_tile_mode(const SampleArgs& a, int64_t row,
   }
 }
 
+// Offers of a staged tile to the part's candidate buffer: each lane marks
+// its values at or above the threshold value (slot layout of read_step), one
+// warp scan sizes the appends, and each lane writes the keys of its marks.
+// A value equal to the threshold value whose key does not beat the threshold
+// leaves a zero key, squeezed out before the count is committed.  When the
+// marks would overflow the buffer even after a compaction (a first tile of
+// near-equal values), the tile is offered step by step instead.
+template <typename S, int KC>
+__device__ __forceinline__ uint32_t mark_tile(const float* buf, float tau_x) {
+  constexpr int VW = Vec<S>::VW;
+  const int lane = threadIdx.x & 31;
+  uint32_t mk = 0;
+#pragma unroll
+  for (int j = 0; j < 32 / VW; ++j) {
+    float x[VW];
+    read_step<S>(buf, j, lane, x);
+#pragma unroll
+    for (int c = 0; c < VW; ++c)
+      if (x[c] > -INFINITY && x[c] >= tau_x) mk |= 1u << (j * VW + c);
+  }
+  return mk;
+}
+
+template <typename S, int KC>
+__device__ __forceinline__ void offer_tile(const float* buf, int start, PartState& ps, StreamMem<KC>* wm) {
+  constexpr int VW = Vec<S>::VW;
+  constexpr int CAP = StreamMem<KC>::CAP;
+  const int lane = threadIdx.x & 31;
+  uint32_t mk = mark_tile<S, KC>(buf, ps.cd.tau_x);
+  int total = (int)__reduce_add_sync(kFull, (unsigned)__popc(mk));
+  if (ps.cd.cnt + total > CAP && ps.cd.cnt > ps.K) {
+    cand_compact<CAP>(wm->cand, wm->hist, ps.cd, ps.K);
+    ps.published = true;
+    mk = mark_tile<S, KC>(buf, ps.cd.tau_x);
+    total = (int)__reduce_add_sync(kFull, (unsigned)__popc(mk));
+  }
+  if (ps.cd.cnt + total > CAP) {
+#pragma unroll 1
+    for (int j = 0; j < 32 / VW; ++j) {
+      float x[VW];
+      read_step<S>(buf, j, lane, x);
+      float lmax = x[0];
+#pragma unroll
+      for (int c = 1; c < VW; ++c) lmax = fmaxf(lmax, x[c]);
+      if (cand_offer_vec<VW, CAP>(x, lmax, (uint32_t)(start + j * 32 * VW + lane * VW), wm->cand, wm->hist, ps.cd,
+                                  ps.K))
+        ps.published = true;
+    }
+    return;
+  }
+  const int n = __popc(mk);
+  const int c0 = ps.cd.cnt;
+  int pos = c0 + warp_incl_scan(n) - n;
+  bool hole = false;
+  while (mk) {
+    const int sl = __ffs(mk) - 1;
+    mk &= mk - 1;
+    const int e = slot_to_elem<VW>(sl, lane);
+    const uint64_t key = rankkey(read_elem<S>(buf, e), (uint32_t)(start + e));
+    const bool ok = key > ps.cd.tau;
+    hole |= !ok;
+    wm->cand[pos++] = ok ? key : 0ull;
+  }
+  __syncwarp();
+  if (__any_sync(kFull, hole)) {
+    const unsigned below = (1u << lane) - 1u;
+    int w = c0;
+    for (int r0 = c0; r0 < c0 + total; r0 += 32) {
+      const int i = r0 + lane;
+      const uint64_t k = i < c0 + total ? wm->cand[i] : 0ull;
+      const unsigned bal = __ballot_sync(kFull, k != 0ull);
+      __syncwarp();
+      if (k) wm->cand[w + __popc(bal & below)] = k;
+      w += __popc(bal);
+      __syncwarp();
+    }
+    total = w - c0;
+  }
+  ps.cd.cnt = c0 + total;
+  if (ps.cd.cnt > ps.K + 128) {
+    cand_compact<CAP>(wm->cand, wm->hist, ps.cd, ps.K);
+    ps.published = true;
+  }
+}
+
+// Approximate sum of one tile held in registers (ApproxStat): the values'
+// ex2(fl(x L - mL)), added pairwise in fp32 -- five levels in the lane (the
+// f32x2 halves, then the two halves), five over the warp, identical in every
+// lane.  mL = fl(m L) of the tile maximum m (finite).
+__device__ __forceinline__ float approx_tile_sum(const float (&v)[32], float mL) {
+  const uint64_t L2 = pk(kLog2eF, kLog2eF), M2 = pk(-mL, -mL);
+  uint64_t w[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint64_t t = fma2(pk(v[2 * i], v[2 * i + 1]), L2, M2);
+    w[i] = pk(ex2_approx(lo_f(t)), ex2_approx(hi_f(t)));
+  }
+#pragma unroll
+  for (int h = 8; h >= 1; h >>= 1)
+#pragma unroll
+    for (int i = 0; i < h; ++i) w[i] = add2(w[i], w[i + h]);
+  float s = fadd(lo_f(w[0]), hi_f(w[0]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s = fadd(s, __shfl_xor_sync(kFull, s, o));
+  return s;
+}
+
+// A whole (or -inf padded ragged) unmasked tile of a filtered row, values of
+// type S in buf: the tile in registers, its maxima and its exact or
+// approximate statistics; then the first-tile bound and the offers, which
+// re-read the staged tile (rarely: most tiles hold nothing above the
+// threshold).
+template <typename S, int KC>
+__device__ __forceinline__ void scan_dense_cand(const SampleArgs& a, int64_t row, int tile, const float* buf,
+                                                PartState& ps, StreamMem<KC>* wm) {
+  constexpr int VW = Vec<S>::VW;
+  const int lane = threadIdx.x & 31;
+  const int start = tile * kTile;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32 / VW; ++j) {
+    float x[VW];
+    read_step<S>(buf, j, lane, x);
+#pragma unroll
+    for (int c = 0; c < VW; ++c) v[j * VW + c] = x[c];
+  }
+  // quarter maxima: quarter q of a lane is its slots 8q .. 8q + 7
+  float h[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float a0 = fmaxf(v[8 * q], v[8 * q + 1]), a1 = fmaxf(v[8 * q + 2], v[8 * q + 3]);
+    const float a2 = fmaxf(v[8 * q + 4], v[8 * q + 5]), a3 = fmaxf(v[8 * q + 6], v[8 * q + 7]);
+    h[q] = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+  }
+  const float lm = fmaxf(fmaxf(h[0], h[1]), fmaxf(h[2], h[3]));
+  float m = -INFINITY;
+  if (ps.needx || ps.needa || ps.minp_floor) m = warp_max(lm);
+  if (ps.minp_floor && m > -INFINITY) {
+    // min-p rows: the tile's own maximum raises the floor before its offers
+    ps.floor = fmaxf(ps.floor, fsub(fadd(m, ps.p.log_min_p), 1.0f));
+    raise_to_floor(ps);
+  }
+  if (ps.needx) {
+    uint64_t sum = 0;
+    if (m > -INFINITY) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        uint64_t q0, q1;
+        q52x2(fsub(v[2 * i], m), fsub(v[2 * i + 1], m), q0, q1);
+        sum += q0 + q1;
+      }
+    }
+    sum = warp_sum_u64(sum);
+    if (lane == 0) { TileStat t; t.m = m; t.pad = 0; t.s = sum; a.statx[row * a.n_tiles + tile] = t; }
+  } else if (ps.needa) {
+    float sa = 0.0f;
+    if (!(m < INFINITY)) sa = __int_as_float(0x7fc00000);  // +inf / NaN: the merge sends the row to the exact pass
+    else if (m > -INFINITY) sa = approx_tile_sum(v, fmul(m, kLog2eF));
+    if (lane == 0) {
+      ApproxStat t;
+      t.m = m;
+      t.s = sa;
+      t.pad = 0;
+      reinterpret_cast<ApproxStat*>(a.staty)[row * a.n_tiles + tile] = t;
+    }
+  }
+  if (ps.cd.tau == 0 && ps.K <= 128) {
+    // the part's first offers: the K-th largest of the tile's 128 quarter
+    // maxima bounds the part's K-th largest value from below, and so does its
+    // upper 16 key bits padded with zeros; the offers start there instead of
+    // at nothing.  Warp search, two bits a step.
+    uint32_t kq[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) kq[q] = h[q] > -INFINITY ? ordkey(h[q]) >> 16 : 0u;
+    uint32_t T = 0;
+#pragma unroll
+    for (int b = 14; b >= 0; b -= 2) {
+      const uint32_t c1 = T | (1u << b), c2 = T | (2u << b), c3 = T | (3u << b);
+      unsigned n1 = 0, n2 = 0, n3 = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        n1 += kq[q] >= c1 ? 1u : 0u;
+        n2 += kq[q] >= c2 ? 1u : 0u;
+        n3 += kq[q] >= c3 ? 1u : 0u;
+      }
+      const uint32_t d = ((int)__reduce_add_sync(kFull, n1) >= ps.K ? 1u : 0u) +
+                         ((int)__reduce_add_sync(kFull, n2) >= ps.K ? 1u : 0u) +
+                         ((int)__reduce_add_sync(kFull, n3) >= ps.K ? 1u : 0u);
+      T |= d << b;
+    }
+    if (T) {
+      ps.cd.tau = (uint64_t)(T << 16) << 32;
+      ps.cd.tau_x = key_value(ps.cd.tau);
+      ps.cd.trimmed = true;
+      ps.published = true;
+    }
+  }
+  if (__any_sync(kFull, lm > -INFINITY && lm >= ps.cd.tau_x)) offer_tile<S, KC>(buf, start, ps, wm);
+}
+
 // Statistics and candidate search of one staged tile, values of type S in buf.
 template <typename S, int KC>
 __device__ __forceinline__ void scan_tile(const SampleArgs& a, int64_t row, int tile, float* buf,
@@ -432,6 +634,11 @@ __device__ __forceinline__ void scan_tile(const SampleArgs& a, int64_t row, int 
   const int lane = threadIdx.x & 31;
   const int n_valid = tile_valid(a, tile);
   const bool masked = a.mask != nullptr;
+  if (!masked && ps.mode == kCand) {
+    // ragged tiles too: the staged buffer is padded with -inf
+    scan_dense_cand<S, KC>(a, row, tile, buf, ps, wm);
+    return;
+  }
   if (!masked && n_valid == kTile) {
     if (ps.mode == kGreedy) scan_tile_mode<S, kGreedy, KC>(a, row, tile, buf, true, ~0u, ps, wm);
     else if (ps.mode == kCand) scan_tile_mode<S, kCand, KC>(a, row, tile, buf, true, ~0u, ps, wm);
@@ -510,7 +717,8 @@ struct MergeCta {
   int scal[8];
   int wcnt[8];
   int wtrim[8];
-  float lse;
+  float lse, lse_hi;  // exact log-sum-exp, or the bracket [lse, lse_hi]
+  int bracket_ok;
 };
 
 template <typename T, int KC>
@@ -539,7 +747,8 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
     }
     const int K = (p.top_k > 0 && p.top_k < KC) ? p.top_k : KC;
     const bool needx = needs_xstats(a, p, mode);
-    // 1. warp 0: the row log-sum-exp.  Warps 1..7 (fw = wid - 1): parts fw,
+    const bool needa = needs_astats(a, p, mode);
+    // 1. warp 0: the row log-sum-exp (or its bracket).  Warps 1..7 (fw = wid - 1): parts fw,
     //    fw + 7, ... into their own top-K, from the row's shared threshold; a
     //    round takes 32 of the warp's parts at once (lane i: part
     //    fw + 7 (p0 + i)), their keys flattened and loaded eight per lane in
@@ -549,6 +758,11 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
         float mx;
         const float c = warp_combine(a.statx + row * a.n_tiles, a.n_tiles, &mx);
         if (lane == 0) mc->lse = c;
+      } else if (needa) {
+        float lo = __int_as_float(0x7fc00000), hi = __int_as_float(0x7fc00000);
+        const bool ok =
+            warp_bracket(reinterpret_cast<const ApproxStat*>(a.staty) + row * a.n_tiles, a.n_tiles, &lo, &hi);
+        if (lane == 0) { mc->lse = lo; mc->lse_hi = hi; mc->bracket_ok = ok; }
       }
       if (lane == 0) { mc->wcnt[0] = 0; mc->wtrim[0] = 0; }
     } else {
@@ -640,12 +854,16 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
     __syncthreads();
     // 4. filters and draw
     if (wid == 0) {
-      const float c = needx ? mc->lse : __int_as_float(0x7fc00000);
+      const float c = (needx || needa) ? mc->lse : __int_as_float(0x7fc00000);
+      const float c_hi = needa ? mc->lse_hi : __int_as_float(0x7fc00000);
       int ns = 0;
-      float x_tok;
-      const int tok = warp_filter_draw(a, p, row, mc->carry, ncarry, !dropped, c, &ns, mc->score, &x_tok);
+      float x_tok = -INFINITY;
+      const int tok = (needa && !mc->bracket_ok)
+                          ? -2
+                          : warp_filter_draw(a, p, row, mc->carry, ncarry, !dropped, c, &ns, mc->score, &x_tok, c_hi);
+      if (tok == -2) queue_exact<KC>(a, row, mc->carry, ncarry);
       if (tok >= 0 && a.surv_ids && lane == 0) write_survivors(a, p, row, mc->carry, ns);
-      if (lane == 0) write_row(a, row, mode, tok, x_tok, c, ns);
+      if (lane == 0) write_row(a, row, mode, tok, x_tok, needa ? __int_as_float(0x7fc00000) : c, ns);
     }
     __syncthreads();
   }
@@ -674,6 +892,94 @@ __global__ void __launch_bounds__(256) k_row_merge_warp(const __grid_constant__ 
     if (lane == 0) write_row(a, row, row_mode(row_params(a, row)), tok, x_tok, lse, ns);
     __syncwarp();
   }
+}
+
+// The exact pass over the rows whose top-p cut the bracket left open (queued
+// by the merges): the grid's warps take the queued rows' tiles in turn and
+// write their exact statistics; the warp that writes a row's last tile (a
+// counter per queue entry) finishes the row as the merge would have with the
+// exact log-sum-exp -- the cut over the row's saved top candidates, the
+// draw, the outputs.  With an empty queue every CTA returns after one load.
+template <typename T, int KC>
+struct ExactMem {
+  float wbuf[kTile];
+  uint64_t S[KC];
+};
+
+template <typename T, int KC>
+__global__ void __launch_bounds__(256) k_row_exact(const __grid_constant__ SampleArgs a) {
+  constexpr int VW = Lay<T>::VW;
+  extern __shared__ __align__(128) unsigned char smem_exact[];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int n = ld_cg(&a.exact_q[0]);
+  if (n == 0) return;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  ExactMem<T, KC>* xm = reinterpret_cast<ExactMem<T, KC>*>(smem_exact) + wid;
+  int32_t* done = a.exact_q + 1;
+  const int32_t* queue = a.exact_q + 1 + a.rows;
+  const int64_t total = (int64_t)n * a.n_tiles;
+  for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < total; g += (int64_t)gridDim.x * 8) {
+    const int q = (int)(g / a.n_tiles);
+    const int t = (int)(g - (int64_t)q * a.n_tiles);
+    const int64_t row = ld_cg(&queue[q]);
+    const pm_row_params p = row_params(a, row);
+    TileIn ti;
+    load_tile<T>(a, row, t, ti);
+    process_tile<VW>(a, p, row, t, ti, xm->wbuf);
+    float m;
+    uint64_t s;
+    tile_stats(ti.v, &m, &s);
+    if (lane == 0) {
+      TileStat st;
+      st.m = m;
+      st.pad = 0;
+      st.s = s;
+      a.statx[row * a.n_tiles + t] = st;
+    }
+    __threadfence();
+    int prev = 0;
+    if (lane == 0) prev = atomicAdd(&done[q], 1);
+    prev = __shfl_sync(kFull, prev, 0);
+    if (prev != a.n_tiles - 1) continue;
+    __threadfence();
+    float mx;
+    const float c = warp_combine(a.statx + row * a.n_tiles, a.n_tiles, &mx);
+    const int nc = ld_cg(&a.cand_n[row * a.max_parts]);
+    const uint64_t* src = a.cand + row * a.max_parts * (int64_t)KC;
+    for (int i = lane; i < nc; i += 32) xm->S[i] = ld_cg(&src[i]);
+    __syncwarp();
+    int ns = 0;
+    float x_tok = -INFINITY;
+    const int tok = warp_filter_draw(a, p, row, xm->S, nc, true, c, &ns, nullptr, &x_tok);
+    if (tok >= 0 && a.surv_ids && lane == 0) write_survivors(a, p, row, xm->S, ns);
+    if (lane == 0) write_row(a, row, kCand, tok, x_tok, c, ns);
+    __syncwarp();
+  }
+}
+
+// Largest relative error of ex2_approx over every fp32 a in [-126, 1]
+// against the fp64 2^a: a grid-stride walk over the bit patterns of
+// [-126, -0] and of [+0, 1]; the maximum (a non-negative double, so its bits
+// order like unsigned integers) is folded in with one atomicMax per warp.
+__global__ void __launch_bounds__(256) k_selfcheck_ex2(unsigned long long* out) {
+  const uint32_t neg_lo = 0x80000000u, neg_hi = 0xC2FC0000u;  // -0 .. -126
+  const uint32_t pos_hi = 0x3F800000u;                        // +0 .. 1
+  const uint64_t n_neg = (uint64_t)(neg_hi - neg_lo) + 1, n_all = n_neg + (uint64_t)pos_hi + 1;
+  double worst = 0.0;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_all;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t bits = i < n_neg ? neg_lo + (uint32_t)i : (uint32_t)(i - n_neg);
+    const float a = __uint_as_float(bits);
+    const double ref = exp2((double)a);
+    const double err = fabs((double)ex2_approx(a) - ref) / ref;
+    worst = err > worst ? err : worst;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double t = __shfl_xor_sync(kFull, worst, o);
+    worst = t > worst ? t : worst;
+  }
+  if ((threadIdx.x & 31) == 0) atomicMax(out, (unsigned long long)__double_as_longlong(worst));
 }
 
 // The streaming kernel.  Warp gw owns the flattened tiles
@@ -896,7 +1202,7 @@ int occupancy_for(int dtype, int KC) {
 struct Layout {
   int n_tiles = 0, KC = 0, ovr_cap = 0, max_parts = 0;
   int64_t n_warps = 0;
-  size_t row_tau = 0, status = 0, statx = 0, staty = 0, cand = 0, cand_n = 0, best = 0, ovr_tok = 0,
+  size_t row_tau = 0, status = 0, exact = 0, statx = 0, staty = 0, cand = 0, cand_n = 0, best = 0, ovr_tok = 0,
          ovr_info = 0, ovr_off = 0, bias_off = 0, row_lse = 0, total = 0;
 };
 
@@ -933,6 +1239,7 @@ int plan(const pm_rows* r, Layout* L) {
   auto take = [&](size_t bytes) { o = align_up(o, 256); const size_t at = o; o += bytes; return at; };
   L->status = take(sizeof(int32_t) * R);
   L->row_tau = take(sizeof(uint64_t) * R);
+  L->exact = take(sizeof(int32_t) * (1 + 2 * R));
   L->statx = take(sizeof(pm::TileStat) * R * L->n_tiles);
   L->staty = take(sizeof(pm::TileStat) * R * L->n_tiles);
   L->cand = take(sizeof(uint64_t) * R * L->max_parts * L->KC);
@@ -983,6 +1290,8 @@ int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::Sample
   a.row_tau = reinterpret_cast<uint64_t*>(ws + L.row_tau);
   a.status = reinterpret_cast<int32_t*>(ws + L.status);
   a.row_lse = reinterpret_cast<float*>(ws + L.row_lse);
+  a.exact_q = reinterpret_cast<int32_t*>(ws + L.exact);
+  a.approx_ok = false;
   a.ovr_tok = nullptr;
   a.ovr_info = nullptr;
   a.ovr_off = nullptr;
@@ -1013,6 +1322,7 @@ int launch_prep(const pm_rows* r, const Layout& L, unsigned char* ws, pm::Sample
     pa.ovr_off = reinterpret_cast<int32_t*>(ws + L.ovr_off);
     pa.status = a.status;
     pa.row_tau = a.row_tau;
+    pa.exact_q = a.exact_q;
     const size_t smem = sizeof(int) * (6 * (size_t)L.ovr_cap + 2 * 264);
     static DeviceOnce once;
     once([&] {
@@ -1049,19 +1359,24 @@ int launch_stream(pm::SampleArgs a, bool cand_rows, cudaStream_t st, bool merge 
   const int64_t grid = (a.n_warps + pm::kWarpsS - 1) / pm::kWarpsS;
   if (grid == 0) return PM_OK;
   cudaError_t e;
-  // the row status (the streaming pass ORs a copy timeout into it) and the
-  // shared row thresholds ("nothing proven") start at zero; the penalty prep
-  // zeroes both when it runs.  The workspace plan puts the thresholds right
-  // after the status array, so one memset covers both.
+  // the row status (the streaming pass ORs a copy timeout into it), the
+  // shared row thresholds ("nothing proven") and the exact pass's queue
+  // count and tile counters start at zero; the penalty prep zeroes all of
+  // them when it runs.  The workspace plan puts the three arrays one after
+  // the other, so one memset covers them.
   if (!a.status_live) {
     const char* s0 = reinterpret_cast<const char*>(a.status);
     const char* t0 = reinterpret_cast<const char*>(a.row_tau);
-    const size_t sb = sizeof(int32_t) * a.rows, tb = sizeof(uint64_t) * a.rows;
-    if (cand_rows && t0 >= s0 + sb && t0 <= s0 + sb + 256) {
-      e = cudaMemsetAsync(a.status, 0, (size_t)(t0 - s0) + tb, st);
+    const char* x0 = reinterpret_cast<const char*>(a.exact_q);
+    const size_t sb = sizeof(int32_t) * a.rows, tb = sizeof(uint64_t) * a.rows,
+                 xb = sizeof(int32_t) * (1 + a.rows);
+    const bool adjacent = t0 >= s0 + sb && t0 <= s0 + sb + 256 && x0 >= t0 + tb && x0 <= t0 + tb + 256;
+    if ((cand_rows || a.approx_ok) && adjacent) {
+      e = cudaMemsetAsync(a.status, 0, (size_t)(x0 - s0) + (a.approx_ok ? xb : 0), st);
     } else {
       e = cudaMemsetAsync(a.status, 0, sb, st);
       if (e == cudaSuccess && cand_rows) e = cudaMemsetAsync(a.row_tau, 0, tb, st);
+      if (e == cudaSuccess && a.approx_ok) e = cudaMemsetAsync(a.exact_q, 0, xb, st);
     }
     if (e != cudaSuccess) return cuda_fail(e);
     a.status_live = true;
@@ -1120,6 +1435,22 @@ int launch_stream(pm::SampleArgs a, bool cand_rows, cudaStream_t st, bool merge 
     cudaGetLastError();  // no programmatic launch here: plain stream order
     if (per_cta) pm::k_row_merge_cta<T, KC><<<(unsigned)mgrid, 256, msmem, st>>>(a);
     else pm::k_row_merge_warp<T, KC><<<(unsigned)mgrid, 256, msmem, st>>>(a);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (!a.approx_ok) return PM_OK;
+  // the exact pass for the rows the bracket left open (usually none)
+  const size_t xsmem = sizeof(pm::ExactMem<T, KC>) * 8;
+  static DeviceOnce xonce;
+  xonce([&] {
+    cudaFuncSetAttribute(pm::k_row_exact<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xsmem);
+  });
+  cfg.gridDim = dim3((unsigned)num_sms());
+  cfg.dynamicSmemBytes = xsmem;
+  e = cudaLaunchKernelEx(&cfg, pm::k_row_exact<T, KC>, a);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    pm::k_row_exact<T, KC><<<(unsigned)num_sms(), 256, xsmem, st>>>(a);
     e = cudaGetLastError();
   }
   return e == cudaSuccess ? PM_OK : cuda_fail(e);
@@ -1323,6 +1654,11 @@ int pm_sample_rows(const pm_rows* rows, const pm_noise* noise, const pm_sample_o
   a.n_surv = out->n_surv;
   a.surv_cap = out->surv_cap;
   a.want_lse = out->lse != nullptr || out->token_logprob != nullptr;
+  // bracketed statistics for top-k + top-p rows when the streaming pass has
+  // at least four tiles a warp (below that it is latency-bound, and the
+  // exact pass's launch would cost more than it saves)
+  a.approx_ok = !a.want_lse && !rows->mask && rows->top_k_max > 0 && (rows->flags_any & PM_F_TOP_P) &&
+                rows->rows * (int64_t)L.n_tiles >= 4 * L.n_warps;
   return launch_rows(rows, L.KC, a, st);
 }
 
@@ -1693,6 +2029,26 @@ int pm_shard_merge(const pm_rows* rows, const pm_shard* shard, const pm_noise* n
   a.n_tiles = m.nt;
   return S.cand_k == 64 ? launch_shard_merge<64>(a, m, reinterpret_cast<cudaStream_t>(stream))
                         : launch_shard_merge<256>(a, m, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int pm_selfcheck_ex2(double* max_rel_err) {
+  if (!max_rel_err) return PM_ERR_ARG;
+  unsigned long long* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, sizeof(unsigned long long));
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = cudaMemset(d, 0, sizeof(unsigned long long));
+  if (e == cudaSuccess) {
+    pm::k_selfcheck_ex2<<<(unsigned)num_sms() * 8, 256>>>(d);
+    e = cudaGetLastError();
+  }
+  unsigned long long bits = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&bits, d, sizeof(bits), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (e != cudaSuccess) return cuda_fail(e);
+  double v;
+  memcpy(&v, &bits, sizeof(v));
+  *max_rel_err = v;
+  return PM_OK;
 }
 
 }  // extern "C"

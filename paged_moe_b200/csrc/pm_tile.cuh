@@ -21,6 +21,18 @@ struct TileStat {
   uint64_t s;     // sum over the tile of floor(e^(x - m) 2^52)
 };
 
+// Approximate statistics of one tile (rows whose filters need the log-sum-exp
+// only to place the top-p cut): m as in TileStat and
+// s ~ sum over the tile of 2^(fl(x L - fl(m L))), L = fl32(log2 e), from the
+// hardware ex2 and fp32 sums.  Stored in the row's y-statistics slots, which
+// such rows do not use.
+struct ApproxStat {
+  float m;
+  float s;
+  uint64_t pad;
+};
+static_assert(sizeof(ApproxStat) == sizeof(TileStat), "ApproxStat shares the TileStat slots");
+
 // Everything the streaming kernels read or write.
 struct SampleArgs {
   const void* logits;
@@ -65,6 +77,13 @@ struct SampleArgs {
   int32_t* status;   // [rows] 0 ok, 1 survivors beyond the candidates, 2 history window too long
   bool status_live;  // status[] already holds this call's flags (zeroed, or written by the penalty prep)
   float* row_lse;    // [rows]
+  // bracketed statistics: rows with top-k and top-p (no min-p) need the
+  // log-sum-exp only to place the top-p cut; with approx_ok the streaming
+  // pass writes approximate tile sums for them, the merge places the cut from
+  // a rigorous bracket around the exact log-sum-exp, and the rare rows whose
+  // cut the bracket does not decide are queued for the exact pass
+  bool approx_ok;
+  int32_t* exact_q;  // [1 + 2 rows]: queued count, per-entry tile counters [rows], queued rows [rows]
   int32_t n_tiles;
   int32_t max_parts;
   int64_t n_warps;   // warps of the launch (the flattened tile range is split over them)
@@ -234,8 +253,14 @@ __device__ __forceinline__ bool minp_floor_row(const pm_row_params& p) {
   return (p.flags & PM_F_MIN_P) && !(p.flags & PM_F_TOP_P) && p.top_k <= 0 && p.min_tokens_to_keep <= 1;
 }
 
+// Rows whose exact log-sum-exp is replaced by a bracket (see SampleArgs).
+__device__ __forceinline__ bool needs_astats(const SampleArgs& a, const pm_row_params& p, int mode) {
+  return a.approx_ok && !a.want_lse && !a.mask && mode == kCand && p.top_k > 0 && (p.flags & PM_F_TOP_P) &&
+         !(p.flags & PM_F_MIN_P);
+}
+
 __device__ __forceinline__ bool needs_xstats(const SampleArgs& a, const pm_row_params& p, int mode) {
-  return a.want_lse || (mode == kCand && (p.flags & (PM_F_TOP_P | PM_F_MIN_P)));
+  return a.want_lse || (mode == kCand && (p.flags & (PM_F_TOP_P | PM_F_MIN_P)) && !needs_astats(a, p, mode));
 }
 
 // Flattened split of rows * n_tiles tiles over n_warps warps: warp w owns

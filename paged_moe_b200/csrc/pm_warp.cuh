@@ -231,6 +231,62 @@ __device__ __forceinline__ float warp_combine(const TileStat* st, int nt, float*
   return combine_lane_tiles<true>(lt, m);
 }
 
+// Bracket [*c_lo, *c_hi] around the fp32 log-sum-exp that warp_combine
+// returns from the row's exact statistics, computed from its approximate
+// tile sums (ApproxStat).  Error budget, relative to the row's sum of e^x:
+//   per tile, eps_t = 3e-6 + 2.1e-8 |m_t|, covering the hardware ex2 (2^-20),
+//   the rounding of each exponent argument a (2^-24 |a| per value, and
+//   sum v|a| <= 20.02 s over at most 1024 values), L != log2 e
+//   (1.34e-8 |x|, with sum v|x| <= s (|m_t| + 13.9)), and the ten levels of
+//   fp32 additions (12 2^-24);
+//   the exact statistics differ from the true log-sum-exp by at most 1.3e-6
+//   before their final fp32 rounding (rounding of x - m_t, 14.02 2^-24 by
+//   the same bound; two ulps of the fp32 exponential; the floors).
+// The bracket is rounded outward and widened by one more ulp each side.
+// Returns false when a statistic is not finite (the row takes the exact pass).
+__device__ __forceinline__ bool warp_bracket(const ApproxStat* st, int nt, float* c_lo, float* c_hi) {
+  const int lane = threadIdx.x & 31;
+  float mt[kMaxPer], sv[kMaxPer];
+  float mx = -INFINITY;
+  bool bad = false;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int t = lane * kMaxPer + i;
+    mt[i] = t < nt ? ld_cg(&st[t].m) : -INFINITY;
+    sv[i] = t < nt ? ld_cg(&st[t].s) : 0.0f;
+    bad |= !(mt[i] == mt[i]) || !(sv[i] == sv[i]) || sv[i] == INFINITY;
+    mx = fmaxf(mx, mt[i]);
+  }
+  mx = warp_max(mx);
+  if (__any_sync(kFull, bad) || mx == INFINITY) return false;
+  if (mx == -INFINITY) {  // no finite value: the exact statistics give -inf
+    *c_lo = *c_hi = -INFINITY;
+    return true;
+  }
+  const float ML = fmul(mx, kLog2eF);
+  double z = 0.0, e = 0.0;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    if (mt[i] > -INFINITY && sv[i] > 0.0f) {
+      const double d = dsub((double)fmul(mt[i], kLog2eF), (double)ML);
+      const double w = dmul((double)sv[i], det_exp64(dmul(d, 0x1.62e42fefa39efp-1)));
+      z = dadd(z, w);
+      e = dfma(w, dfma(2.1e-8, (double)fabsf(mt[i]), 3e-6), e);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    z = dadd(z, __shfl_xor_sync(kFull, z, o));
+    e = dadd(e, __shfl_xor_sync(kFull, e, o));
+  }
+  if (!(z > 0.0) || !(z < 1e300)) return false;
+  const double lse = dadd(dmul((double)ML, 0x1.62e42fefa39efp-1), det_log64(z));
+  const double half = 1.0001 * (e / z) + 1.3e-6 + 1e-12 * fabs(lse);
+  *c_lo = nextafterf(__double2float_rd(lse - half), -INFINITY);
+  *c_hi = nextafterf(__double2float_ru(lse + half), INFINITY);
+  return true;
+}
+
 __device__ __forceinline__ float row_gumbel(const SampleArgs& a, int64_t row, uint32_t token) {
   if (a.noise_mode == PM_NOISE_INJECTED) return a.gumbel[row * a.gumbel_stride + token];
   return philox_gumbel(a.seed, a.offset, a.row_base + (uint32_t)row, token);
@@ -253,9 +309,12 @@ __device__ __forceinline__ uint64_t row_u53(const SampleArgs& a, int64_t row, in
 // Returns the token, or -1 when the survivors reach past the candidates (the
 // row is then flagged; only possible when top_k is off).  *n_out = survivors;
 // *x_out (when given) = the token's value, S's value at its rank.
+// With c_hi given (not NaN), [c, c_hi] brackets the exact log-sum-exp (top-k
+// rows, see warp_bracket): the cut is the one every value in the bracket
+// gives, or the call returns -2 when the bracket does not decide it.
 __device__ inline int warp_filter_draw(const SampleArgs& a, const pm_row_params& p, int64_t row, const uint64_t* S,
                                 int m, bool complete, float c, int* n_out, const float* scores = nullptr,
-                                float* x_out = nullptr) {
+                                float* x_out = nullptr, float c_hi = __builtin_nanf("")) {
   const int lane = threadIdx.x & 31;
   *n_out = 0;
   if (x_out) *x_out = -INFINITY;
@@ -263,7 +322,46 @@ __device__ inline int warp_filter_draw(const SampleArgs& a, const pm_row_params&
   const bool topk = p.top_k > 0;
   int cnt = (topk && p.top_k < m) ? p.top_k : m;
   bool determined = topk || complete;
-  if (p.flags & PM_F_TOP_P) {
+  if ((p.flags & PM_F_TOP_P) && topk && c_hi == c_hi && c_hi != c) {
+    // Tails T - A_r at c_hi bound the exact ones from below, at c from above
+    // (the fp32 exponential is monotone up to two ulps, and each q52 floors:
+    // margins of 2^-18 relative and 2 cnt + 2 absolute).  Rank r is kept
+    // for sure when the lower bound clears the threshold, dropped for sure
+    // when the upper one does not; the exact cut is then the first rank not
+    // kept for sure, provided that rank is dropped for sure.
+    const uint64_t qthr = __float2ull_rz(fmul(p.top_p_comp, 0x1p52f));
+    const uint64_t slack = 2ull * (uint64_t)cnt + 2ull;
+    uint64_t Th = 0, Tl = 0;
+    for (int r = lane; r < cnt; r += 32) {
+      const float x = key_value(S[r]);
+      Th += q52(fsub(x, c_hi));
+      Tl += q52(fsub(x, c));
+    }
+    Th = warp_sum_u64(Th);
+    Tl = warp_sum_u64(Tl);
+    uint64_t ch = 0, cl = 0;
+    int k_keep = cnt, k_drop = cnt;
+    bool f_keep = false, f_drop = false;
+    for (int base = 0; base < cnt && !(f_keep && f_drop); base += 32) {
+      const int r = base + lane;
+      const float x = r < cnt ? key_value(S[r]) : 0.0f;
+      const uint64_t qh = r < cnt ? q52(fsub(x, c_hi)) : 0ull;
+      const uint64_t ql = r < cnt ? q52(fsub(x, c)) : 0ull;
+      const uint64_t ih = warp_incl_scan_u64(qh), il = warp_incl_scan_u64(ql);
+      const uint64_t tail_h = Th - (ch + ih - qh), tail_l = Tl - (cl + il - ql);
+      uint64_t lower = tail_h - (tail_h >> 18);
+      lower = lower > slack ? lower - slack : 0ull;
+      const uint64_t upper = tail_l + (tail_l >> 18) + slack;
+      const unsigned nk = __ballot_sync(kFull, r < cnt && !(lower > qthr));
+      const unsigned nd = __ballot_sync(kFull, r < cnt && upper <= qthr);
+      if (!f_keep && nk) { k_keep = base + __ffs(nk) - 1; f_keep = true; }
+      if (!f_drop && nd) { k_drop = base + __ffs(nd) - 1; f_drop = true; }
+      ch += __shfl_sync(kFull, ih, 31);
+      cl += __shfl_sync(kFull, il, 31);
+    }
+    if (k_keep != k_drop) return -2;
+    cnt = k_keep < 1 ? 1 : k_keep;
+  } else if (p.flags & PM_F_TOP_P) {
     // q52 of the first 64 ranks once, kept for the cut search below
     const uint64_t qa = lane < cnt ? q52(fsub(key_value(S[lane]), c)) : 0ull;
     const uint64_t qb = lane + 32 < cnt ? q52(fsub(key_value(S[lane + 32]), c)) : 0ull;
@@ -492,6 +590,21 @@ __device__ __forceinline__ bool part_trimmed(const SampleArgs& a, int64_t row, i
   return !(minp && rt && ld_cg(&a.best[row * a.max_parts + part]) <= rt);
 }
 
+// A row whose top-p cut the bracket left open: its sorted top candidates go
+// to the row's first part slot and the row into the exact pass's queue.
+template <int KC>
+__device__ __forceinline__ void queue_exact(const SampleArgs& a, int64_t row, const uint64_t* S, int n) {
+  const int lane = threadIdx.x & 31;
+  uint64_t* dst = a.cand + row * a.max_parts * (int64_t)KC;
+  for (int i = lane; i < n; i += 32) dst[i] = S[i];
+  if (lane == 0) {
+    a.cand_n[row * a.max_parts] = n;
+    const int q = atomicAdd(&a.exact_q[0], 1);
+    a.exact_q[1 + a.rows + q] = (int32_t)row;
+  }
+  __syncwarp();
+}
+
 // Row merge by the warp that completed the row: gathers the parts' results
 // and draws the token.  Returns the token (-1 when flagged); *x_tok the
 // chosen token's processed logit, *lse the row log-sum-exp (NaN if unused).
@@ -501,10 +614,13 @@ __device__ __noinline__ int warp_row_merge(const SampleArgs& a, int64_t row, int
   const int lane = threadIdx.x & 31;
   const pm_row_params p = row_params(a, row);
   const int mode = row_mode(p);
-  float c = __int_as_float(0x7fc00000);
+  float c = __int_as_float(0x7fc00000), c_hi = __int_as_float(0x7fc00000);
   float mx;
+  bool bracket_ok = true;
   if (needs_xstats(a, p, mode)) c = warp_combine(a.statx + row * a.n_tiles, a.n_tiles, &mx);
-  *lse_out = c;
+  else if (needs_astats(a, p, mode))
+    bracket_ok = warp_bracket(reinterpret_cast<const ApproxStat*>(a.staty) + row * a.n_tiles, a.n_tiles, &c, &c_hi);
+  *lse_out = c_hi == c_hi ? __int_as_float(0x7fc00000) : c;
   *n_surv_out = 0;
   int tok = 0;
   *x_tok = -INFINITY;
@@ -568,9 +684,13 @@ __device__ __noinline__ int warp_row_merge(const SampleArgs& a, int64_t row, int
     if (cd.cnt > K) cand_compact<CAP>(cbuf, hist, cd, K);
     warp_sort_desc(cbuf, cd.cnt);
     int ns = 0;
-    tok = warp_filter_draw(a, p, row, cbuf, cd.cnt, !(trimmed_any || cd.trimmed), c, &ns);
+    tok = bracket_ok ? warp_filter_draw(a, p, row, cbuf, cd.cnt, !(trimmed_any || cd.trimmed), c, &ns, nullptr,
+                                        nullptr, c_hi)
+                     : -2;
     *n_surv_out = ns;
-    if (tok >= 0) {
+    if (tok == -2) {
+      queue_exact<KC>(a, row, cbuf, cd.cnt);
+    } else if (tok >= 0) {
       for (int r = 0; r < cd.cnt; ++r)
         if ((int)key_index(cbuf[r]) == tok) { *x_tok = key_value(cbuf[r]); break; }
       if (a.surv_ids && lane == 0) write_survivors(a, p, row, cbuf, ns);
@@ -585,7 +705,7 @@ __device__ __noinline__ int warp_row_merge(const SampleArgs& a, int64_t row, int
 __device__ __forceinline__ void write_row(const SampleArgs& a, int64_t row, int mode, int tok, float x_tok,
                                           float lse, int ns) {
   const int32_t prevs = a.status_live ? ld_cg(&a.status[row]) : 0;
-  a.status[row] = prevs | (tok < 0 ? 1 : 0);
+  a.status[row] = prevs | (tok == -2 ? 64 : tok < 0 ? 1 : 0);
   a.tokens[row] = tok;
   if (a.lse_out) a.lse_out[row] = lse;
   if (a.row_lse) a.row_lse[row] = lse;
