@@ -56,6 +56,13 @@ struct PartState {
   bool minp_floor;
   float floor;
   uint64_t fkey;    // the floor as a key (what these rows publish)
+  // approximate statistics (needa): per lane, a compensated sum of the
+  // part's 2^(x L - aLref) against a warp-uniform reference, and the lane's
+  // maximum; nres counts the reference's moves
+  int t0;           // the part's first tile in its row
+  float aref, aLref;
+  float as_hi, as_c, amx;
+  int nres;
 };
 
 __device__ __forceinline__ void part_begin(const SampleArgs& a, int64_t row, int first_tile, int KC,
@@ -74,6 +81,11 @@ __device__ __forceinline__ void part_begin(const SampleArgs& a, int64_t row, int
   ps.minp_floor = minp_floor_row(ps.p);
   ps.floor = -INFINITY;
   ps.fkey = 0;
+  ps.t0 = first_tile;
+  ps.aref = ps.aLref = -INFINITY;
+  ps.as_hi = ps.as_c = 0.0f;
+  ps.amx = -INFINITY;
+  ps.nres = 0;
 }
 
 // The threshold a part shares with the other parts of its row: the K-th
@@ -512,12 +524,11 @@ __device__ __forceinline__ void offer_tile(const float* buf, int start, PartStat
   }
 }
 
-// Approximate sum of one tile held in registers (ApproxStat): the values'
-// ex2(fl(x L - mL)), added pairwise in fp32 -- five levels in the lane (the
-// f32x2 halves, then the two halves), five over the warp, identical in every
-// lane.  mL = fl(m L) of the tile maximum m (finite).
-__device__ __forceinline__ float approx_tile_sum(const float (&v)[32], float mL) {
-  const uint64_t L2 = pk(kLog2eF, kLog2eF), M2 = pk(-mL, -mL);
+// One lane's approximate partial of a tile held in registers: the sum of
+// ex2(fl(x L - aLref)) over its 32 values, added pairwise in fp32 -- four
+// levels over the f32x2 halves, then the two halves.
+__device__ __forceinline__ float approx_lane_sum(const float (&v)[32], float aLref) {
+  const uint64_t L2 = pk(kLog2eF, kLog2eF), M2 = pk(-aLref, -aLref);
   uint64_t w[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
@@ -528,10 +539,66 @@ __device__ __forceinline__ float approx_tile_sum(const float (&v)[32], float mL)
   for (int h = 8; h >= 1; h >>= 1)
 #pragma unroll
     for (int i = 0; i < h; ++i) w[i] = add2(w[i], w[i + h]);
-  float s = fadd(lo_f(w[0]), hi_f(w[0]));
+  return fadd(lo_f(w[0]), hi_f(w[0]));
+}
+
+// A tile's share of the part's approximate statistics (lm: the lane's
+// maximum of the tile).  The reference is the first finite tile maximum; it
+// moves up (the sums rescaled by the hardware ex2 of the step) when a value
+// would sit more than 2^64 above it.  A non-finite reference poisons the sum
+// (NaN), which sends the row to the exact pass.
+__device__ __forceinline__ void approx_tile(const float (&v)[32], float lm, PartState& ps) {
+  if (!(ps.aLref > -INFINITY)) {
+    const float m = warp_max(lm);
+    if (!(m > -INFINITY)) return;  // nothing finite yet
+    ps.aref = m;
+    ps.aLref = fmul(m, kLog2eF);
+    if (!(m < INFINITY)) ps.as_hi = __int_as_float(0x7fc00000);
+  } else if (__any_sync(kFull, ffma(lm, kLog2eF, -ps.aLref) > 64.0f)) {
+    const float m = warp_max(lm);
+    const float nL = fmul(m, kLog2eF);
+    const float f = ex2_approx(fsub(ps.aLref, nL));
+    ps.as_hi = fmul(ps.as_hi, f);
+    ps.as_c = fmul(ps.as_c, f);
+    ps.aref = m;
+    ps.aLref = nL;
+    ps.nres += 1;
+    if (!(m < INFINITY)) ps.as_hi = __int_as_float(0x7fc00000);
+  }
+  // Kahan summation of the tile partials
+  const float t = approx_lane_sum(v, ps.aLref);
+  const float y = fsub(t, ps.as_c);
+  const float u = fadd(ps.as_hi, y);
+  ps.as_c = fsub(fsub(u, ps.as_hi), y);
+  ps.as_hi = u;
+  ps.amx = fmaxf(ps.amx, lm);
+}
+
+// The part's approximate statistics at its end (lane 0 writes them to the
+// slot of its first tile).  Relative error bound of s, with N <= 8192
+// values a lane (A = 25: N A 2^-A < 0.01 of the largest term):
+//   hardware ex2                                 2^-20
+//   exponent arguments, |rho| <= 2^-24 |a| and
+//   sum v|a| <= (A + 0.01 + |a_top|) s           2^-24 ln2 (25.01 + |a_top|)
+//   L != log2 e, |x| <= |m_part| + A / L          1.4e-8 (|m_part| + 18)
+//   four-level tree, halves, Kahan                8 2^-24
+//   each move of the reference                    1.2e-6, and |a| up to 64 + A
+// (a_top: the part maximum's argument against the final reference).
+__device__ __forceinline__ void approx_part_end(const SampleArgs& a, int64_t row, const PartState& ps) {
+  double s = (double)ps.as_hi + (double)ps.as_c;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s = fadd(s, __shfl_xor_sync(kFull, s, o));
-  return s;
+  for (int o = 16; o > 0; o >>= 1) s = dadd(s, __shfl_xor_sync(kFull, s, o));
+  const float mp = warp_max(ps.amx);
+  if ((threadIdx.x & 31) == 0) {
+    const float atop = fabsf(ffma(mp, kLog2eF, -ps.aLref));
+    const float argb = ps.nres ? 64.0f + 25.01f : 25.01f + atop;
+    ApproxStat st;
+    st.mref = ps.aref;
+    st.eps = (float)(0x1p-20 + 0x1p-24 * 0.6931471805599453 * (double)argb +
+                     1.4e-8 * ((double)fabsf(mp) + 18.0) + 8.0 * 0x1p-24 + 1.2e-6 * ps.nres);
+    st.s = ps.aLref > -INFINITY ? s : 0.0;
+    reinterpret_cast<ApproxStat*>(a.staty)[row * a.n_tiles + ps.t0] = st;
+  }
 }
 
 // A whole (or -inf padded ragged) unmasked tile of a filtered row, values of
@@ -563,7 +630,7 @@ __device__ __forceinline__ void scan_dense_cand(const SampleArgs& a, int64_t row
   }
   const float lm = fmaxf(fmaxf(h[0], h[1]), fmaxf(h[2], h[3]));
   float m = -INFINITY;
-  if (ps.needx || ps.needa || ps.minp_floor) m = warp_max(lm);
+  if (ps.needx || ps.minp_floor) m = warp_max(lm);
   if (ps.minp_floor && m > -INFINITY) {
     // min-p rows: the tile's own maximum raises the floor before its offers
     ps.floor = fmaxf(ps.floor, fsub(fadd(m, ps.p.log_min_p), 1.0f));
@@ -582,16 +649,7 @@ __device__ __forceinline__ void scan_dense_cand(const SampleArgs& a, int64_t row
     sum = warp_sum_u64(sum);
     if (lane == 0) { TileStat t; t.m = m; t.pad = 0; t.s = sum; a.statx[row * a.n_tiles + tile] = t; }
   } else if (ps.needa) {
-    float sa = 0.0f;
-    if (!(m < INFINITY)) sa = __int_as_float(0x7fc00000);  // +inf / NaN: the merge sends the row to the exact pass
-    else if (m > -INFINITY) sa = approx_tile_sum(v, fmul(m, kLog2eF));
-    if (lane == 0) {
-      ApproxStat t;
-      t.m = m;
-      t.s = sa;
-      t.pad = 0;
-      reinterpret_cast<ApproxStat*>(a.staty)[row * a.n_tiles + tile] = t;
-    }
+    approx_tile(v, lm, ps);
   }
   if (ps.cd.tau == 0 && ps.K <= 128) {
     // the part's first offers: the K-th largest of the tile's 128 quarter
@@ -684,6 +742,7 @@ __device__ __forceinline__ void part_end(const SampleArgs& a, int64_t row, int64
     const uint64_t wk = warp_max_u64(k);
     if (lane == 0) a.best[row * a.max_parts + part] = wk;
   } else if (ps.mode == kCand) {
+    if (ps.needa) approx_part_end(a, row, ps);
     if (ps.cd.cnt > ps.K) cand_compact<CAP>(wm->cand, wm->hist, ps.cd, ps.K);
     // the part's final threshold bounds the row's K-th key (or its min-p
     // cut) from below: the merge starts from the largest one
@@ -760,8 +819,7 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
         if (lane == 0) mc->lse = c;
       } else if (needa) {
         float lo = __int_as_float(0x7fc00000), hi = __int_as_float(0x7fc00000);
-        const bool ok =
-            warp_bracket(reinterpret_cast<const ApproxStat*>(a.staty) + row * a.n_tiles, a.n_tiles, &lo, &hi);
+        const bool ok = warp_bracket(a, row, n_parts, &lo, &hi);
         if (lane == 0) { mc->lse = lo; mc->lse_hi = hi; mc->bracket_ok = ok; }
       }
       if (lane == 0) { mc->wcnt[0] = 0; mc->wtrim[0] = 0; }

@@ -21,15 +21,15 @@ struct TileStat {
   uint64_t s;     // sum over the tile of floor(e^(x - m) 2^52)
 };
 
-// Approximate statistics of one tile (rows whose filters need the log-sum-exp
-// only to place the top-p cut): m as in TileStat and
-// s ~ sum over the tile of 2^(fl(x L - fl(m L))), L = fl32(log2 e), from the
-// hardware ex2 and fp32 sums.  Stored in the row's y-statistics slots, which
-// such rows do not use.
+// Approximate statistics of one row part (rows whose filters need the
+// log-sum-exp only to place the top-p cut): s ~ sum over the part of
+// 2^(fl(x L - fl(mref L))), L = fl32(log2 e), from the hardware ex2 and fp32
+// sums, with eps a bound on its relative error.  Stored in the row's
+// y-statistics slot of the part's first tile (such rows use no y statistics).
 struct ApproxStat {
-  float m;
-  float s;
-  uint64_t pad;
+  float mref;   // the part's reference value (-inf: the part holds no finite value)
+  float eps;
+  double s;
 };
 static_assert(sizeof(ApproxStat) == sizeof(TileStat), "ApproxStat shares the TileStat slots");
 

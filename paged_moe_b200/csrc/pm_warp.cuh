@@ -136,6 +136,44 @@ __device__ __forceinline__ void warp_sort_desc(uint64_t* S, int m) {
   }
 }
 
+// Bitonic sort of 32 E keys held in registers, descending: element i is
+// k[i / 32] of lane i % 32.  Partners less than 32 apart are exchanged by
+// shuffles, the others inside the lane.
+template <int E>
+__device__ __forceinline__ void warp_sort_regs_desc(uint64_t (&k)[E]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int kk = 2; kk <= 32 * E; kk <<= 1) {
+#pragma unroll
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      uint64_t y[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) y[e] = j < 32 ? __shfl_xor_sync(kFull, k[e], j) : k[e ^ (j >> 5)];
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const int i = e * 32 + lane;
+        const bool want_max = ((i & j) == 0) == ((i & kk) == 0);
+        k[e] = want_max ? (k[e] > y[e] ? k[e] : y[e]) : (k[e] < y[e] ? k[e] : y[e]);
+      }
+    }
+  }
+}
+
+// The K largest of buf[0..n) (n <= 128, K <= n) sorted descending into
+// buf[0..K), through registers.
+__device__ __forceinline__ void warp_top_sorted_128(uint64_t* buf, int n, int K) {
+  const int lane = threadIdx.x & 31;
+  uint64_t k[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) k[e] = e * 32 + lane < n ? buf[e * 32 + lane] : 0ull;
+  __syncwarp();
+  warp_sort_regs_desc<4>(k);
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    if (e * 32 + lane < K) buf[e * 32 + lane] = k[e];
+  __syncwarp();
+}
+
 // a_t = s_t e^(m_t - m) of tile t (0 for an empty tile).
 __device__ __forceinline__ double tile_weight(const TileStat* st, int t, float m) {
   const uint64_t s = ld_cg(&st[t].s);
@@ -232,46 +270,54 @@ __device__ __forceinline__ float warp_combine(const TileStat* st, int nt, float*
 }
 
 // Bracket [*c_lo, *c_hi] around the fp32 log-sum-exp that warp_combine
-// returns from the row's exact statistics, computed from its approximate
-// tile sums (ApproxStat).  Error budget, relative to the row's sum of e^x:
-//   per tile, eps_t = 3e-6 + 2.1e-8 |m_t|, covering the hardware ex2 (2^-20),
-//   the rounding of each exponent argument a (2^-24 |a| per value, and
-//   sum v|a| <= 20.02 s over at most 1024 values), L != log2 e
-//   (1.34e-8 |x|, with sum v|x| <= s (|m_t| + 13.9)), and the ten levels of
-//   fp32 additions (12 2^-24);
-//   the exact statistics differ from the true log-sum-exp by at most 1.3e-6
-//   before their final fp32 rounding (rounding of x - m_t, 14.02 2^-24 by
-//   the same bound; two ulps of the fp32 exponential; the floors).
-// The bracket is rounded outward and widened by one more ulp each side.
-// Returns false when a statistic is not finite (the row takes the exact pass).
-__device__ __forceinline__ bool warp_bracket(const ApproxStat* st, int nt, float* c_lo, float* c_hi) {
+// returns from the row's exact statistics, computed from its parts'
+// approximate statistics (ApproxStat, with their relative error bounds eps_p):
+//   Z = sum_p s_p 2^(fl(mref_p L) - ML),  lse = ML ln2 + ln Z,
+//   |ln(true sum) - lse| <= 1.0001 sum_p w_p eps_p / Z;
+// the exact statistics differ from the true log-sum-exp by at most 1.3e-6
+// before their final fp32 rounding (rounding of x - m_t, 14.02 2^-24 by the
+// bound sum e^d |d| <= 14.02 sum e^d over a tile; two ulps of the fp32
+// exponential; the floors).  The bracket is rounded outward and widened by
+// one more ulp each side.  Returns false when a part's sum is not finite
+// (the row takes the exact pass).
+__device__ __forceinline__ bool warp_bracket(const SampleArgs& a, int64_t row, int n_parts, float* c_lo,
+                                             float* c_hi) {
   const int lane = threadIdx.x & 31;
-  float mt[kMaxPer], sv[kMaxPer];
-  float mx = -INFINITY;
+  const int64_t T = a.rows * a.n_tiles, base = row * a.n_tiles;
+  const int64_t w0 = owner_warp(base, T, a.n_warps);
+  const ApproxStat* st = reinterpret_cast<const ApproxStat*>(a.staty) + base;
+  float ml = -INFINITY;
   bool bad = false;
-#pragma unroll
-  for (int i = 0; i < kMaxPer; ++i) {
-    const int t = lane * kMaxPer + i;
-    mt[i] = t < nt ? ld_cg(&st[t].m) : -INFINITY;
-    sv[i] = t < nt ? ld_cg(&st[t].s) : 0.0f;
-    bad |= !(mt[i] == mt[i]) || !(sv[i] == sv[i]) || sv[i] == INFINITY;
-    mx = fmaxf(mx, mt[i]);
+  for (int p0 = 0; p0 < n_parts; p0 += 32) {
+    const int p = p0 + lane;
+    if (p < n_parts) {
+      const int64_t g0 = (w0 + p) * T / a.n_warps;
+      const int t0 = (int)(g0 > base ? g0 - base : 0);
+      const float mr = ld_cg(&st[t0].mref);
+      const double sv = ld_cg(&st[t0].s);
+      bad |= !(sv == sv) || !(sv < 1e300) || !(mr == mr) || mr == INFINITY;
+      if (mr > -INFINITY) ml = fmaxf(ml, fmul(mr, kLog2eF));
+    }
   }
-  mx = warp_max(mx);
-  if (__any_sync(kFull, bad) || mx == INFINITY) return false;
-  if (mx == -INFINITY) {  // no finite value: the exact statistics give -inf
+  ml = warp_max(ml);
+  if (__any_sync(kFull, bad)) return false;
+  if (ml == -INFINITY) {  // no finite value: the exact statistics give -inf
     *c_lo = *c_hi = -INFINITY;
     return true;
   }
-  const float ML = fmul(mx, kLog2eF);
   double z = 0.0, e = 0.0;
-#pragma unroll
-  for (int i = 0; i < kMaxPer; ++i) {
-    if (mt[i] > -INFINITY && sv[i] > 0.0f) {
-      const double d = dsub((double)fmul(mt[i], kLog2eF), (double)ML);
-      const double w = dmul((double)sv[i], det_exp64(dmul(d, 0x1.62e42fefa39efp-1)));
-      z = dadd(z, w);
-      e = dfma(w, dfma(2.1e-8, (double)fabsf(mt[i]), 3e-6), e);
+  for (int p0 = 0; p0 < n_parts; p0 += 32) {
+    const int p = p0 + lane;
+    if (p < n_parts) {
+      const int64_t g0 = (w0 + p) * T / a.n_warps;
+      const int t0 = (int)(g0 > base ? g0 - base : 0);
+      const float mr = ld_cg(&st[t0].mref);
+      if (mr > -INFINITY) {
+        const double d = dsub((double)fmul(mr, kLog2eF), (double)ml);
+        const double w = dmul(ld_cg(&st[t0].s), det_exp64(dmul(d, 0x1.62e42fefa39efp-1)));
+        z = dadd(z, w);
+        e = dfma(w, (double)ld_cg(&st[t0].eps), e);
+      }
     }
   }
 #pragma unroll
@@ -280,7 +326,7 @@ __device__ __forceinline__ bool warp_bracket(const ApproxStat* st, int nt, float
     e = dadd(e, __shfl_xor_sync(kFull, e, o));
   }
   if (!(z > 0.0) || !(z < 1e300)) return false;
-  const double lse = dadd(dmul((double)ML, 0x1.62e42fefa39efp-1), det_log64(z));
+  const double lse = dadd(dmul((double)ml, 0x1.62e42fefa39efp-1), det_log64(z));
   const double half = 1.0001 * (e / z) + 1.3e-6 + 1e-12 * fabs(lse);
   *c_lo = nextafterf(__double2float_rd(lse - half), -INFINITY);
   *c_hi = nextafterf(__double2float_ru(lse + half), INFINITY);
@@ -619,7 +665,7 @@ __device__ __noinline__ int warp_row_merge(const SampleArgs& a, int64_t row, int
   bool bracket_ok = true;
   if (needs_xstats(a, p, mode)) c = warp_combine(a.statx + row * a.n_tiles, a.n_tiles, &mx);
   else if (needs_astats(a, p, mode))
-    bracket_ok = warp_bracket(reinterpret_cast<const ApproxStat*>(a.staty) + row * a.n_tiles, a.n_tiles, &c, &c_hi);
+    bracket_ok = warp_bracket(a, row, n_parts, &c, &c_hi);
   *lse_out = c_hi == c_hi ? __int_as_float(0x7fc00000) : c;
   *n_surv_out = 0;
   int tok = 0;
@@ -681,18 +727,25 @@ __device__ __noinline__ int warp_row_merge(const SampleArgs& a, int64_t row, int
         for (int u = 0; u < 8; ++u) cand_offer_key<CAP>(keys[u], cbuf, hist, cd, K);
       }
     }
-    if (cd.cnt > K) cand_compact<CAP>(cbuf, hist, cd, K);
-    warp_sort_desc(cbuf, cd.cnt);
+    if (cd.cnt <= 128) {
+      // few keys (the usual case behind the row threshold): sort them in
+      // registers and keep the first K
+      if (cd.cnt > K) cd.trimmed = true;
+      warp_top_sorted_128(cbuf, cd.cnt, K < cd.cnt ? K : cd.cnt);
+      cd.cnt = K < cd.cnt ? K : cd.cnt;
+    } else {
+      cand_compact<CAP>(cbuf, hist, cd, K);
+      if (cd.cnt <= 128) warp_top_sorted_128(cbuf, cd.cnt, cd.cnt);
+      else warp_sort_desc(cbuf, cd.cnt);
+    }
     int ns = 0;
     tok = bracket_ok ? warp_filter_draw(a, p, row, cbuf, cd.cnt, !(trimmed_any || cd.trimmed), c, &ns, nullptr,
-                                        nullptr, c_hi)
+                                        x_tok, c_hi)
                      : -2;
     *n_surv_out = ns;
     if (tok == -2) {
       queue_exact<KC>(a, row, cbuf, cd.cnt);
     } else if (tok >= 0) {
-      for (int r = 0; r < cd.cnt; ++r)
-        if ((int)key_index(cbuf[r]) == tok) { *x_tok = key_value(cbuf[r]); break; }
       if (a.surv_ids && lane == 0) write_survivors(a, p, row, cbuf, ns);
     }
   } else {
