@@ -51,7 +51,8 @@ def parse():
     ap.add_argument("--c5-rows", type=int, default=1024,
                     help="rows of the C5 workload (smaller only for profiling captures)")
     ap.add_argument("--workload", default="c3",
-                    choices=["c3", "c3u", "c5", "c5e", "c1", "c2", "c2b", "c4a", "c4b", "ngram", "think", "logprobs"],
+                    choices=["c3", "c3u", "c5", "c5e", "c1", "c2", "c2b", "c4a", "c4b", "ngram", "think", "logprobs",
+                             "lmhead"],
                     help="c3 (default): the headline metric's config; c5: C5 rows (one GPU: the unsharded pass; "
                          "torchrun: vocabulary-sharded over the ranks); c5e: eight vocabulary shards emulated on "
                          "one GPU; the rest: the other configs and the path's neighbours (n-gram drafts, "
@@ -663,10 +664,110 @@ def run_config(args):
     print(json.dumps(line), flush=True)
 
 
+def run_lmhead(args):
+    """The LM head fused with the sampler (the logits producer of the
+    reference's decode step, pagedmoe/verify_decode.py:821): 256 rows of
+    hidden size 2,048 into a vocabulary of 151,936 (a Qwen3-30B-A3B-class
+    head; random-init bf16 weights), top_k 50, top_p 0.95 at temp 1, Philox
+    draw.  Timed: the fused call, the unfused pair (the same GEMM writing
+    fp32 logits, then the sampling pass) and cuBLAS's bf16 GEMM alone, each
+    as a CUDA-graph replay.  Roofline: tensor-bound, 2 B H V flops a step
+    against the measured sustained cuBLAS bf16 rate."""
+    import torch
+
+    import paged_moe_b200 as pm
+    from paged_moe_b200 import engine
+    from paged_moe_b200.params import SamplerSettings
+    dev = torch.device("cuda", 0)
+    B, H, V = 256, 2048, 151936
+    gen = torch.Generator(device=dev).manual_seed(7)
+    w = (torch.randn(V, H, device=dev, generator=gen) * 0.05).to(torch.bfloat16)
+    hs = [torch.randn(B, H, device=dev, generator=gen).to(torch.bfloat16) for _ in range(2)]
+    s = SamplerSettings(temp=1.0, top_k=50, top_p=0.95)
+    buf = torch.empty(B, V, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def fused(i):
+        return engine.lmhead_sample(hs[i & 1], w, s, seed=5, offset=i)
+
+    def unfused(i):
+        engine.lmhead_logits(hs[i & 1], w, out=buf)
+        return pm.sample_rows(buf, s, seed=5, offset=i)
+
+    def gemm(i):
+        return engine.lmhead_logits(hs[i & 1], w, out=buf)
+
+    def cublas(i):
+        return hs[i & 1] @ w.T
+
+    def graph_time(fn, n=8, reps=4):
+        for i in range(max(args.warmup, 3)):
+            fn(i)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n):
+                fn(100 + i)
+        g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        del g
+        return e0.elapsed_time(e1) * 1000 / (n * reps)
+
+    # eager steps of the fused call (the headline of this line)
+    for i in range(max(args.warmup, 3)):
+        fused(i)
+    torch.cuda.synchronize(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with Clocks(0) as clk:
+        ev[0].record(stream)
+        for i in range(args.steps):
+            fused(args.warmup + i)
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize(dev)
+        t_fused = graph_time(fused)
+        t_unfused = graph_time(unfused)
+        t_gemm = graph_time(gemm)
+        t_cublas = graph_time(cublas)
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    ms = statistics.mean(per)
+    flops = 2.0 * B * H * V
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tpk, kind = float(json.load(f)["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        tpk, kind = 1400.0, "fallback"
+    ach = flops / (t_fused * 1e-6) / 1e12
+    line = {
+        "metric": "sampled rows/s (LM head fused with the sampler)", "value": B / (ms / 1000.0), "unit": "rows/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 operands, f32 accumulate", "data": "synthetic",
+        "config": {"workload": f"LM head {B} x {H} -> {V} (random-init bf16 weights) + top_k 50, top_p 0.95, "
+                               "temp 1, Philox draw", "l2": "weights 622 MB (> L2), two hidden batches"},
+        "eager_p50_us_per_step": 1000 * statistics.median(per),
+        "graph_us_per_step": t_fused,
+        "unfused_graph_us_per_step": t_unfused,
+        "gemm_only_graph_us": t_gemm,
+        "cublas_bf16_gemm_graph_us": t_cublas,
+        "roofline": {"bound": "tensor", "achieved": ach, "peak": tpk, "unit": "TFLOP/s", "frac": ach / tpk,
+                     "traffic": None, "peak_source": f"{kind} MEASURED_PEAKS.json bf16_tflops_sustained",
+                     "algorithmic_flops_per_launch": flops, "timing": "graph replay"},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "lmhead":
+        run_lmhead(args)
     elif args.workload in ("c5", "c5e"):
         run_c5(args)
     elif args.workload != "c3":

@@ -5,8 +5,11 @@
  * logits processors, the log-softmax, the sampler and the draft acceptance
  * of a verify pass.  All pointers are device pointers unless stated; every
  * function takes a cudaStream_t (as void*) and returns a status code, never
- * aborts, allocates nothing, and keeps no global state, so it may be called
- * from several host threads on different streams with separate workspaces.
+ * aborts and allocates nothing.  The only process-wide state is per device:
+ * each kernel's shared-memory attribute and occupancy, set up on the first
+ * launch on that device, and the scratch array of pm_sample_rows_static.
+ * Calls with separate workspaces may come from several host threads on
+ * different streams.
  *
  * Reference interfaces replaced (paths within noahclark556/paged-moe):
  *   pm_sample_rows      sampler(logprobs) -> tokens, built by mlx-lm's
@@ -250,6 +253,41 @@ PM_API int pm_think_budget(const int32_t *gen, const int32_t *gen_len, int64_t g
                            const int32_t *piece_len, const uint8_t *piece_end, int64_t table_size,
                            const int32_t *chars, const int32_t *close, int32_t n_close, int32_t end_id,
                            int32_t start_id, int32_t slack, int32_t *forced, void *stream);
+
+/* The LM head: logits = hidden @ weight^T on the tensor cores (bf16 in, fp32
+ * accumulate), the producer of the logits that the reference's decode step
+ * computes before its processors and sampler (pagedmoe/verify_decode.py:821,
+ * :824 for a plain step, :887 for a verify pass).  hidden: [n_tokens,
+ * hidden_stride] bf16 (the final-norm output); weight: [vocab,
+ * weight_stride] bf16 (row v: token v's output embedding).  Both 16-byte
+ * aligned with strides a multiple of 8 elements. */
+typedef struct pm_lmhead {
+    const void *hidden;
+    int64_t n_tokens;
+    int64_t hidden_size;
+    int64_t hidden_stride;       /* elements between rows */
+    const void *weight;
+    int64_t weight_stride;       /* elements between rows */
+} pm_lmhead;
+
+/* The logits themselves: [n_tokens, logits_stride] fp32 (stride a multiple
+ * of 4, 16-byte aligned). */
+PM_API int pm_lmhead_logits(const pm_lmhead *h, int64_t vocab, float *logits, int64_t logits_stride,
+                            void *stream);
+
+/* LM head fused with pm_sample_rows: the GEMM's epilogue writes the tile
+ * statistics and candidates of each row, so the logits never reach device
+ * memory; the results are those of pm_sample_rows on the logits that
+ * pm_lmhead_logits computes (tokens, log-sum-exp, survivors, bit for bit).
+ * rows: rows == h->n_tokens and rows->logits unused; greedy rows and rows
+ * with 0 < top_k <= 256 (temperature, top_p and min_p on top), with the
+ * allowed-token mask.  Penalties, logit bias, forced tokens, unbounded
+ * top-p / min-p and whole-vocabulary draws return PM_ERR_UNSUPPORTED (use
+ * pm_lmhead_logits + pm_sample_rows).  Row status bit 128: a logit was NaN or
+ * +inf.  The workspace needs no zeroing. */
+PM_API size_t pm_lmhead_sample_workspace_bytes(const pm_lmhead *h, const pm_rows *rows);
+PM_API int pm_lmhead_sample(const pm_lmhead *h, const pm_rows *rows, const pm_noise *noise,
+                            const pm_sample_out *out, void *workspace, size_t workspace_bytes, void *stream);
 
 /* pm_sample_rows on scratch owned by the library (no counterpart in the
  * reference, which runs on MLX's allocator): for callers that cannot hand

@@ -99,6 +99,13 @@ class ShardArgs(C.Structure):
     ]
 
 
+class LmHead(C.Structure):
+    _fields_ = [
+        ("hidden", C.c_void_p), ("n_tokens", C.c_int64), ("hidden_size", C.c_int64),
+        ("hidden_stride", C.c_int64), ("weight", C.c_void_p), ("weight_stride", C.c_int64),
+    ]
+
+
 # Exported symbols and their signatures: (restype, argtypes)
 _P = C.c_void_p
 SIGNATURES = {
@@ -119,6 +126,9 @@ SIGNATURES = {
     "pm_think_budget": (C.c_int, [_P, _P, C.c_int64, C.c_int64, _P, _P, C.c_int64, _P, _P, C.c_int32, C.c_int32,
                                   C.c_int32, C.c_int32, _P, _P]),
     "pm_draft_ngram": (C.c_int, [_P, _P, C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P]),
+    "pm_lmhead_logits": (C.c_int, [_P, C.c_int64, _P, C.c_int64, _P]),
+    "pm_lmhead_sample_workspace_bytes": (C.c_size_t, [_P, _P]),
+    "pm_lmhead_sample": (C.c_int, [_P, _P, _P, _P, _P, C.c_size_t, _P]),
 }
 
 _lib = None

@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 SO = os.path.join(HERE, "libpm_sample.so")
-SOURCES = ["pm_sample.cu", "pm_masked.cu"]
+SOURCES = ["pm_sample.cu", "pm_masked.cu", "pm_lmhead.cu"]
 OBJDIR = os.path.join(HERE, "_build")
 
 NVCC_FLAGS = [

@@ -87,3 +87,7 @@ struct SampleArgs;
 // The masked gather pass (pm_masked.cu): rows with an allowed-token mask
 // whose logits can be fetched as aligned 4-byte words.
 int pm_launch_masked(int dtype, int KC, const pm::SampleArgs& a, cudaStream_t st);
+
+// The row merges (pm_sample.cu) over parts that a pass of another
+// translation unit wrote (pm_lmhead.cu).
+int pm_launch_merges(int KC, const pm::SampleArgs& a, cudaStream_t st);

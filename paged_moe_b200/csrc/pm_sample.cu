@@ -790,8 +790,9 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int64_t total = a.rows * a.n_tiles;
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
-    const int n_parts = (int)(owner_warp((row + 1) * a.n_tiles - 1, total, a.n_warps) -
-                              owner_warp(row * a.n_tiles, total, a.n_warps) + 1);
+    const int n_parts = a.fixed_parts > 0 ? a.fixed_parts
+                                          : (int)(owner_warp((row + 1) * a.n_tiles - 1, total, a.n_warps) -
+                                                  owner_warp(row * a.n_tiles, total, a.n_warps) + 1);
     const pm_row_params p = row_params(a, row);
     const int mode = row_mode(p);
     if (mode != kCand) {
@@ -830,7 +831,7 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
       const bool minp = minp_floor_row(p);
       const uint64_t rt = ld_cg(&a.row_tau[row]);
       if (rt) {
-        cd.tau = rt;
+        cd.tau = merge_floor(rt);
         cd.tau_x = key_value(rt);
         cd.trimmed = !minp;
       }
@@ -942,8 +943,9 @@ __global__ void __launch_bounds__(256) k_row_merge_warp(const __grid_constant__ 
   const int64_t total = a.rows * a.n_tiles;
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + wid; row < a.rows;
        row += (int64_t)gridDim.x * (blockDim.x >> 5)) {
-    const int n_parts = (int)(owner_warp((row + 1) * a.n_tiles - 1, total, a.n_warps) -
-                              owner_warp(row * a.n_tiles, total, a.n_warps) + 1);
+    const int n_parts = a.fixed_parts > 0 ? a.fixed_parts
+                                          : (int)(owner_warp((row + 1) * a.n_tiles - 1, total, a.n_warps) -
+                                                  owner_warp(row * a.n_tiles, total, a.n_warps) + 1);
     float x_tok, lse;
     int ns;
     const int tok = warp_row_merge<T, KC, CAP>(a, row, n_parts, mm->cand, mm->hist, &x_tok, &lse, &ns);
@@ -1410,6 +1412,63 @@ bool has_cand_rows(const pm_rows* r) {
   return r->top_k_max > 0 || (r->flags_any & (PM_F_TOP_P | PM_F_MIN_P));
 }
 
+// The row merges after a pass that wrote the parts' results, chained by
+// programmatic dependent launch, then the exact pass when the bracket is on.
+template <typename T, int KC>
+int launch_merges(const pm::SampleArgs& a, cudaStream_t st) {
+  cudaError_t e;
+  // the row merges, chained by programmatic dependent launch: one CTA per
+  // row when rows are few (every row then has many parts), one warp per row
+  // otherwise
+  const bool per_cta = a.rows <= (int64_t)num_sms() * 2;
+  const size_t msmem = per_cta ? sizeof(pm::MergeCta<KC>) : (sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * 8;
+  static DeviceOnce once;
+  once([&] {
+    cudaFuncSetAttribute(pm::k_row_merge_cta<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sizeof(pm::MergeCta<KC>));
+    cudaFuncSetAttribute(pm::k_row_merge_warp<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)((sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * 8));
+  });
+  int64_t mgrid = per_cta ? a.rows : (a.rows + 7) / 8;
+  const int64_t mcap = (int64_t)num_sms() * (per_cta ? 3 : 8);
+  if (mgrid > mcap) mgrid = mcap;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)mgrid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = msmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = per_cta ? cudaLaunchKernelEx(&cfg, pm::k_row_merge_cta<T, KC>, a)
+              : cudaLaunchKernelEx(&cfg, pm::k_row_merge_warp<T, KC>, a);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // no programmatic launch here: plain stream order
+    if (per_cta) pm::k_row_merge_cta<T, KC><<<(unsigned)mgrid, 256, msmem, st>>>(a);
+    else pm::k_row_merge_warp<T, KC><<<(unsigned)mgrid, 256, msmem, st>>>(a);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (!a.approx_ok) return PM_OK;
+  // the exact pass for the rows the bracket left open (usually none)
+  const size_t xsmem = sizeof(pm::ExactMem<T, KC>) * 8;
+  static DeviceOnce xonce;
+  xonce([&] {
+    cudaFuncSetAttribute(pm::k_row_exact<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xsmem);
+  });
+  cfg.gridDim = dim3((unsigned)num_sms());
+  cfg.dynamicSmemBytes = xsmem;
+  e = cudaLaunchKernelEx(&cfg, pm::k_row_exact<T, KC>, a);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    pm::k_row_exact<T, KC><<<(unsigned)num_sms(), 256, xsmem, st>>>(a);
+    e = cudaGetLastError();
+  }
+  return e == cudaSuccess ? PM_OK : cuda_fail(e);
+}
+
 template <typename T, int KC>
 int launch_stream(pm::SampleArgs a, bool cand_rows, cudaStream_t st, bool merge = true) {
   stream_occupancy<T, KC>();
@@ -1462,56 +1521,7 @@ int launch_stream(pm::SampleArgs a, bool cand_rows, cudaStream_t st, bool merge 
     }
   }
   if (!merge) return PM_OK;
-  // the row merges, chained by programmatic dependent launch: one CTA per
-  // row when rows are few (every row then has many parts), one warp per row
-  // otherwise
-  const bool per_cta = a.rows <= (int64_t)num_sms() * 2;
-  const size_t msmem = per_cta ? sizeof(pm::MergeCta<KC>) : (sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * 8;
-  static DeviceOnce once;
-  once([&] {
-    cudaFuncSetAttribute(pm::k_row_merge_cta<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)sizeof(pm::MergeCta<KC>));
-    cudaFuncSetAttribute(pm::k_row_merge_warp<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)((sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * 8));
-  });
-  int64_t mgrid = per_cta ? a.rows : (a.rows + 7) / 8;
-  const int64_t mcap = (int64_t)num_sms() * (per_cta ? 3 : 8);
-  if (mgrid > mcap) mgrid = mcap;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)mgrid);
-  cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = msmem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = per_cta ? cudaLaunchKernelEx(&cfg, pm::k_row_merge_cta<T, KC>, a)
-              : cudaLaunchKernelEx(&cfg, pm::k_row_merge_warp<T, KC>, a);
-  if (e != cudaSuccess) {
-    cudaGetLastError();  // no programmatic launch here: plain stream order
-    if (per_cta) pm::k_row_merge_cta<T, KC><<<(unsigned)mgrid, 256, msmem, st>>>(a);
-    else pm::k_row_merge_warp<T, KC><<<(unsigned)mgrid, 256, msmem, st>>>(a);
-    e = cudaGetLastError();
-  }
-  if (e != cudaSuccess) return cuda_fail(e);
-  if (!a.approx_ok) return PM_OK;
-  // the exact pass for the rows the bracket left open (usually none)
-  const size_t xsmem = sizeof(pm::ExactMem<T, KC>) * 8;
-  static DeviceOnce xonce;
-  xonce([&] {
-    cudaFuncSetAttribute(pm::k_row_exact<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xsmem);
-  });
-  cfg.gridDim = dim3((unsigned)num_sms());
-  cfg.dynamicSmemBytes = xsmem;
-  e = cudaLaunchKernelEx(&cfg, pm::k_row_exact<T, KC>, a);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    pm::k_row_exact<T, KC><<<(unsigned)num_sms(), 256, xsmem, st>>>(a);
-    e = cudaGetLastError();
-  }
-  return e == cudaSuccess ? PM_OK : cuda_fail(e);
+  return launch_merges<T, KC>(a, st);
 }
 
 int launch_stream_any(int dtype, int KC, const pm::SampleArgs& a, bool cand_rows, cudaStream_t st) {
@@ -1671,6 +1681,13 @@ int launch_accept(const pm::SampleArgs& a, int dtype, const pm::VerifyK& vk, int
 }
 
 }  // namespace
+
+// The row merges over parts written by another translation unit's pass (the
+// fused LM-head pass): rows never take the whole-vocabulary draw there, so
+// the logits type is immaterial.
+int pm_launch_merges(int KC, const pm::SampleArgs& a, cudaStream_t st) {
+  return KC == 64 ? launch_merges<float, 64>(a, st) : launch_merges<float, 256>(a, st);
+}
 
 extern "C" {
 

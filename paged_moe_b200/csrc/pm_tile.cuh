@@ -87,6 +87,7 @@ struct SampleArgs {
   int32_t n_tiles;
   int32_t max_parts;
   int64_t n_warps;   // warps of the launch (the flattened tile range is split over them)
+  int32_t fixed_parts;  // > 0: every row has this many parts (the fused LM-head pass's vocabulary slices)
   // verify extension (pm_verify.cu); rows are requests * (k+1) target rows
   int32_t feed_group;
   void* verify;      // VerifyState* or null

@@ -19,6 +19,14 @@ struct Cand {
   uint64_t ctau;  // the last compaction's threshold (keys it dropped lie below)
 };
 
+// The threshold an empty merge buffer starts from so that it accepts every
+// key at or above the row's shared bound rt.  A published bound is either a
+// part's own K-th key (a real key, which that part's list holds, so the
+// buffer must admit it: start one below) or a synthetic value threshold with
+// zero low bits (a min-p floor, the first-tile estimate), which no real key
+// equals.
+__device__ __forceinline__ uint64_t merge_floor(uint64_t rt) { return (rt & 0xFFFFFFFFull) ? rt - 1 : rt; }
+
 __device__ __forceinline__ void cand_reset(Cand& c) {
   c.cnt = 0;
   c.tau = 0;
@@ -687,7 +695,7 @@ __device__ __noinline__ int warp_row_merge(const SampleArgs& a, int64_t row, int
     const bool minp = minp_floor_row(p);
     const uint64_t rt = ld_cg(&a.row_tau[row]);
     if (rt) {
-      cd.tau = rt;
+      cd.tau = merge_floor(rt);
       cd.tau_x = key_value(rt);
       cd.trimmed = !minp;
     }

@@ -360,3 +360,85 @@ def argmax_confidence(logits: torch.Tensor, processors=None, history=None, mask=
                       return_logprob=True)
     return res["tokens"], torch.exp(res["logprob"])
 
+
+
+def _lmhead_struct(hidden: torch.Tensor, weight: torch.Tensor, keep: _Keep) -> L.LmHead:
+    if hidden.dim() != 2 or weight.dim() != 2 or hidden.shape[1] != weight.shape[1]:
+        raise ValueError("hidden must be [tokens, hidden_size] and weight [vocab, hidden_size]")
+    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("the LM head takes bf16 hidden states and weights")
+    if not (hidden.is_cuda and weight.is_cuda) or hidden.device != weight.device:
+        raise ValueError("hidden and weight must be on the same CUDA device")
+    h = hidden if hidden.stride(1) == 1 and hidden.stride(0) % 8 == 0 else keep(hidden.contiguous())
+    w = weight if weight.stride(1) == 1 and weight.stride(0) % 8 == 0 else keep(weight.contiguous())
+    s = L.LmHead()
+    s.hidden, s.n_tokens, s.hidden_size, s.hidden_stride = h.data_ptr(), h.shape[0], h.shape[1], h.stride(0)
+    s.weight, s.weight_stride = w.data_ptr(), w.stride(0)
+    return s
+
+
+def lmhead_logits(hidden: torch.Tensor, weight: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """logits = hidden @ weight.T (bf16 in, fp32 accumulate) on the tensor
+    cores: the LM head of the reference's decode step (pagedmoe/
+    verify_decode.py:821, :887).  The same kernel as lmhead_sample, so these
+    are the logits the fused call samples from."""
+    keep = _Keep()
+    lib = L.load()
+    s = _lmhead_struct(hidden, weight, keep)
+    V = weight.shape[0]
+    if out is None:
+        out = torch.empty((hidden.shape[0], (V + 3) // 4 * 4), dtype=torch.float32, device=hidden.device)[:, :V]
+    stream = torch.cuda.current_stream(hidden.device)
+    rc = lib.pm_lmhead_logits(C.byref(s), V, out.data_ptr(), out.stride(0), stream.cuda_stream)
+    L.check(rc, "pm_lmhead_logits")
+    return out
+
+
+def lmhead_sample(hidden: torch.Tensor, weight: torch.Tensor,
+                  sampler: Union[SamplerSettings, Sequence[SamplerSettings]] = None,
+                  mask: Optional[torch.Tensor] = None, seed: int = 0, offset: int = 0, row_base: int = 0,
+                  gumbel: Optional[torch.Tensor] = None, return_lse: bool = False, return_logprob: bool = False,
+                  survivors: int = 0, return_status: bool = False):
+    """The LM head fused with the sampler: the tokens (and the other outputs
+    of sample_rows) that sample_rows would give on lmhead_logits(hidden,
+    weight), with the logits never written to device memory.  Greedy rows and
+    rows with top_k (plus temperature, top_p, min_p) and an optional mask;
+    other settings raise (use lmhead_logits + sample_rows)."""
+    keep = _Keep()
+    lib = L.load()
+    s = _lmhead_struct(hidden, weight, keep)
+    dev = hidden.device
+    B, V = hidden.shape[0], weight.shape[0]
+    # the rows need a [B, V] logits view only for their shape: one row, broadcast
+    stand_in = torch.empty((1, V), dtype=torch.float32, device=dev).expand(B, V)
+    r = build_rows(stand_in, sampler, None, None, None, mask, keep)
+    r.logits = None
+    n = _noise(B, V, seed, offset, row_base, gumbel, None, keep, dev)
+    o = L.SampleOut()
+    tokens = torch.empty(B, dtype=torch.int32, device=dev)
+    o.tokens = tokens.data_ptr()
+    res = {"tokens": tokens}
+    if return_lse:
+        res["lse"] = torch.empty(B, dtype=torch.float32, device=dev)
+        o.lse = res["lse"].data_ptr()
+    if return_logprob:
+        res["logprob"] = torch.empty(B, dtype=torch.float32, device=dev)
+        o.token_logprob = res["logprob"].data_ptr()
+    if survivors:
+        res["surv_ids"] = torch.empty((B, survivors), dtype=torch.int32, device=dev)
+        res["surv_probs"] = torch.empty((B, survivors), dtype=torch.float32, device=dev)
+        res["n_surv"] = torch.empty(B, dtype=torch.int32, device=dev)
+        o.surv_ids, o.surv_probs, o.n_surv = (res["surv_ids"].data_ptr(), res["surv_probs"].data_ptr(),
+                                              res["n_surv"].data_ptr())
+        o.surv_cap = survivors
+    nbytes = lib.pm_lmhead_sample_workspace_bytes(C.byref(s), C.byref(r))
+    if nbytes == 0:
+        L.check(L.PM_ERR_UNSUPPORTED, "pm_lmhead_sample_workspace_bytes")
+    stream = torch.cuda.current_stream(dev)
+    ws = workspace(nbytes, dev, stream)
+    rc = lib.pm_lmhead_sample(C.byref(s), C.byref(r), C.byref(n), C.byref(o), ws.data_ptr(), ws.numel(),
+                              stream.cuda_stream)
+    L.check(rc, "pm_lmhead_sample")
+    if return_status:
+        res["status"] = status_view(ws, r)
+    return res

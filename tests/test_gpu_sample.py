@@ -202,3 +202,22 @@ def test_unbounded_filters_bf16_with_processors():
     p = ProcessorSettings(repetition_penalty=1.2, repetition_context_size=200, logit_bias=((7, 3.0), (32999, 2.5)))
     ref, got = run_both(None, SamplerSettings(temp=0.9, top_p=0.9), p, hist=hist, bf16=bits)
     assert_same(ref, got)
+
+
+@pytest.mark.parametrize("s", [SamplerSettings(temp=1.0, top_k=1), SamplerSettings(temp=0.9, top_k=1, top_p=0.5),
+                               SamplerSettings(temp=1.0, top_k=50, top_p=0.95),
+                               SamplerSettings(temp=1.0, top_k=64, min_p=0.02)])
+@pytest.mark.parametrize("B", [8, 320])
+def test_row_topk_held_by_one_part(s, B):
+    # rows whose K largest values sit in one tile (and so in one part of the
+    # row): the bound that part publishes is the row's own K-th key, which
+    # the merge must still admit; top_k = 1 makes every row such a row.
+    # B = 8 takes the one-CTA-per-row merge, B = 320 the one-warp-per-row one.
+    rng = np.random.default_rng(77 + B)
+    V = 151936
+    x = (rng.standard_normal((B, V)) * 2.0).astype(np.float32)
+    for b in range(B):
+        t = int(rng.integers(0, V // 1024))
+        x[b, t * 1024 + 100: t * 1024 + 100 + 80] += 12.0
+    ref, got = run_both(x, s, seed=B, surv=16)
+    assert_same(ref, got, surv=16)
