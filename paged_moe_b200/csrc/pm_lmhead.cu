@@ -166,6 +166,10 @@ __device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void st_cluster_u64(uint32_t addr, uint64_t v) {
   asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
 }
@@ -191,11 +195,19 @@ constexpr uint32_t lm_idesc() {
 
 namespace pm {
 
-// Bin of a value below the maximum mh of its half slice: quarter units of
-// mh - x, the last bin collecting everything 15.75 or more below.
-__device__ __forceinline__ int value_bin(float x, float mh) {
-  const float d = fmul(fsub(mh, x), 4.0f);
-  return d < (float)(kLBins - 1) ? (int)d : kLBins - 1;
+// Edges of the candidate histogram below the tile maximum m: e_b = fl(m -
+// (b + 1) / 4), non-increasing in b.  Bin b holds e_b <= x < e_{b-1}; the
+// last bin everything below e_62.
+__device__ __forceinline__ float tile_edge(float m, int b) { return fsub(m, 0.25f * (float)(b + 1)); }
+
+__device__ __forceinline__ int tile_bin(float x, float m) {
+  const float d = fmul(fsub(m, x), 4.0f);
+  int b = d < (float)(kLBins - 1) ? (int)d : kLBins - 1;
+  // settle the estimate on the edges (usually no step): afterwards
+  // bin(x) <= b exactly when x >= e_b, for every b < 63
+  while (b < kLBins - 1 && x < tile_edge(m, b)) ++b;
+  while (b > 0 && x >= tile_edge(m, b - 1)) --b;
+  return b;
 }
 
 struct LmParams {
@@ -325,9 +337,11 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
     // chunk c of the row's processed values: ids past the vocabulary and
     // disallowed ids (bit j of the row's mask word (id0 >> 5) + c) are -inf
     const uint32_t* mrow = (a.mask && vrow) ? a.mask + row * a.mask_stride + (id0 >> 5) : nullptr;
+    const bool plain = a.mask == nullptr;  // uniform: no mask words to apply
     auto chunk = [&](int c, float (&v)[32]) {
       const uint32_t w = mrow ? __ldg(mrow + c) : 0xFFFFFFFFu;
       tmem_ld32(tl + c * 32, v);
+      if (plain && c * 32 + 32 <= hcols) return;
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         if (!((w >> j) & 1u) || c * 32 + j >= hcols) v[j] = -INFINITY;
@@ -372,7 +386,22 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
 #pragma unroll
     for (int q = 0; q < kLCluster; ++q) m = fmaxf(m, sh->xmax[q][r_local]);
 
-    // pass B: integer sum of q52(x - m) over the half
+    // pass B: integer sum of q52(x - m) over the half and, for filtered
+    // rows, a 64-bin histogram of the values by the tile's exact edges
+    // e_b = m - (b + 1) / 4 (bin(x) <= b exactly when x >= e_b)
+    const bool candrow = vrow && mode == kCand;
+    const int K = (p.top_k > 0 && p.top_k < KC) ? p.top_k : KC;
+    uint32_t* hist = reinterpret_cast<uint32_t*>(stages);  // [bin / 4][thread], 8-bit counts (<= 128)
+    const bool binned = candrow && nfin > KC;
+    // values below the row's shared threshold cannot move the tile's bound
+    // above it, so only the values at or above it are binned
+    float bfloor = INFINITY;
+    if (binned) {
+      const uint64_t rt = ld_cg(&a.row_tau[row]);
+      bfloor = rt ? key_value(rt) : -INFINITY;
+    }
+    if (binned)
+      for (int b4 = 0; b4 < kLBins / 4; ++b4) hist[b4 * kLThreads + tid] = 0;
     uint64_t s = 0;
 #pragma unroll 1
     for (int c = 0; c < nch; ++c) {
@@ -386,43 +415,107 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
           s += q0 + q1;
         }
       }
-    }
-    st_cluster_u64(cluster_addr(&sh->xsum[rank * 2 + half][r_local], 0), s);
-    cluster_sync_all();
-    if (rank == 0 && half == 0 && vrow) {
-      uint64_t tot = 0;
+      if (binned) {
 #pragma unroll
-      for (int q = 0; q < 2 * kLCluster; ++q) tot += sh->xsum[q][r_local];
-      TileStat t;
-      t.m = m;
-      t.pad = 0;
-      t.s = m > -INFINITY ? tot : 0ull;
-      a.statx[row * a.n_tiles + tile] = t;
-    }
-    if (vrow && mode == kGreedy) a.best[row * a.max_parts + part] = bk;
-
-    // candidates of filtered rows, one list per half slice (a row part):
-    //   path 1: every finite key (at most KC of them);
-    //   path 2: the keys at or above the row's shared threshold (when at most KC);
-    //   path 3: the keys whose value lies within the quarter-unit bin of the
-    //           half's K-th largest value (one histogram pass), when at most KC;
-    //   path 4: exactly the half's top K (radix select over the ordered keys).
-    // Paths 3 and 4 raise the row's threshold: by the smallest listed key
-    // (at least K keys of the half are at or above it) or the K-th key.
-    const bool candrow = vrow && mode == kCand;
-    const int K = (p.top_k > 0 && p.top_k < KC) ? p.top_k : KC;
-    int path = 0;
-    uint64_t tau = 0;
-    if (candrow) {
-      if (nfin <= KC) {
-        path = 1;
-      } else {
-        tau = ld_cg(&a.row_tau[row]);
-        path = tau ? 2 : 3;
+        for (int j = 0; j < 32; ++j)
+          if (v[j] > -INFINITY && v[j] >= bfloor) {
+            const int b = tile_bin(v[j], m);
+            hist[(b >> 2) * kLThreads + tid] += 1u << ((b & 3) * 8);
+          }
       }
     }
+    // partial sums and histograms to rank 0 ([rank * 2 + half][bin / 4][row]
+    // words in its stage buffers past the local histograms)
+    st_cluster_u64(cluster_addr(&sh->xsum[rank * 2 + half][r_local], 0), s);
+    uint32_t* hx = reinterpret_cast<uint32_t*>(stages + 16384);
+    const int hi = (int)rank * 2 + half;
+#pragma unroll
+    for (int b4 = 0; b4 < kLBins / 4; ++b4)
+      st_cluster_u32(cluster_addr(&hx[(hi * (kLBins / 4) + b4) * kLM + r_local], 0), binned ? hist[b4 * kLThreads + tid] : 0u);
+    cluster_sync_all();
+    // rank 0: the tile's statistics, and its bound for filtered rows -- the
+    // edge of the first bin where the tile's count reaches K (a synthetic key,
+    // low bits 0: at least K keys of the tile lie at or above it), sent to
+    // every CTA of the cluster and raised into the row's shared threshold
+    uint64_t* tb = reinterpret_cast<uint64_t*>(stages + 16384 + 65536);  // [row]: tile bound
+    int32_t* bs = reinterpret_cast<int32_t*>(tb + kLM);                   // [row]: its bin
+    if (rank == 0 && half == 0) {
+      if (vrow) {
+        uint64_t tot = 0;
+#pragma unroll
+        for (int q = 0; q < 2 * kLCluster; ++q) tot += sh->xsum[q][r_local];
+        TileStat t;
+        t.m = m;
+        t.pad = 0;
+        t.s = m > -INFINITY ? tot : 0ull;
+        a.statx[row * a.n_tiles + tile] = t;
+      }
+      uint64_t tkey = 0;
+      int bstar = kLBins;
+      if (candrow) {
+        int cum = 0;
+        for (int b4 = 0; b4 < kLBins / 4 && bstar == kLBins; ++b4) {
+          uint32_t lo = 0, hi2 = 0;  // bins b4*4 + {0, 2} and {1, 3} in 16-bit lanes
+#pragma unroll
+          for (int q = 0; q < 2 * kLCluster; ++q) {
+            const uint32_t w = hx[(q * (kLBins / 4) + b4) * kLM + r_local];
+            lo += w & 0x00FF00FFu;
+            hi2 += (w >> 8) & 0x00FF00FFu;
+          }
+          const int cnt4[4] = {(int)(lo & 0xFFFF), (int)(hi2 & 0xFFFF), (int)(lo >> 16), (int)(hi2 >> 16)};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int b = b4 * 4 + e;
+            if (bstar == kLBins && b < kLBins - 1) {
+              cum += cnt4[e];
+              if (cum >= K) bstar = b;
+            }
+          }
+        }
+        if (bstar < kLBins - 1) {
+          tkey = (uint64_t)ordkey(tile_edge(m, bstar)) << 32;
+          atomicMax(reinterpret_cast<unsigned long long*>(&a.row_tau[row]), (unsigned long long)tkey);
+        }
+      }
+#pragma unroll
+      for (uint32_t q = 0; q < (uint32_t)kLCluster; ++q) {
+        st_cluster_u64(cluster_addr(&tb[r_local], q), tkey);
+        st_cluster_u32(cluster_addr(&bs[r_local], q), (uint32_t)bstar);
+      }
+    }
+    cluster_sync_all();
+    if (vrow && mode == kGreedy) a.best[row * a.max_parts + part] = bk;
+
+    // candidates of filtered rows, one list per half slice (a row part): the
+    // keys at or above teff = max(tile bound, row threshold); at most KC of
+    // them when every finite key fits, or when the half's count within the
+    // tile bound fits; else a threshold the half proves itself -- the row's
+    // threshold when the keys above it fit, or exactly the half's top K by a
+    // radix select over its keys
+    const uint64_t tkey = tb[r_local];
+    const int bstar = bs[r_local];
+    uint64_t teff = 0;
+    int path = 0;  // 1 keys >= teff fit; 2 count the keys >= teff first; 4 the half's own top K
+    if (candrow) {
+      const uint64_t rt = ld_cg(&a.row_tau[row]);
+      teff = tkey > rt ? tkey : rt;
+      if (nfin <= KC) {
+        path = 1;
+      } else if (tkey) {
+        int le = 0;  // the half's values at or above the tile bound
+        for (int b4 = 0; b4 <= bstar / 4; ++b4) {
+          const uint32_t w = hist[b4 * kLThreads + tid];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) le += (b4 * 4 + e <= bstar) ? (int)((w >> (8 * e)) & 255u) : 0;
+        }
+        path = le <= KC ? 1 : (teff > tkey ? 2 : 4);
+      } else {
+        path = teff ? 2 : 4;
+      }
+    }
+    __syncthreads();  // every thread has read its bin counts before the radix histograms reuse them
     if (__any_sync(kFull, path == 2)) {
-      const bool below = path == 2 && ordkey(mh) < (uint32_t)(tau >> 32);
+      const bool below = path == 2 && ordkey(mh) < (uint32_t)(teff >> 32);
       int over = 0;
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
@@ -431,46 +524,20 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
         if (path == 2 && !below) {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            over += v[j] > -INFINITY && rankkey(v[j], id0 + (uint32_t)(c * 32 + j)) >= tau;
+            over += v[j] > -INFINITY && rankkey(v[j], id0 + (uint32_t)(c * 32 + j)) >= teff;
         }
       }
-      if (path == 2 && over > KC) path = 3;
-    }
-    // per-thread histograms [bin][thread] of 8-bit counts (at most 128 values
-    // a thread) in the stage buffers, which the finished MMAs no longer read
-    uint8_t* hist = reinterpret_cast<uint8_t*>(stages);
-    int bcut = 0;
-    if (__any_sync(kFull, path == 3)) {
-      if (path == 3)
-        for (int b = 0; b < kLBins; ++b) hist[b * kLThreads + tid] = 0;
-#pragma unroll 1
-      for (int c = 0; c < nch; ++c) {
-        float v[32];
-        chunk(c, v);
-        if (path == 3) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (v[j] > -INFINITY) hist[value_bin(v[j], mh) * kLThreads + tid] += 1;
-        }
-      }
-      if (path == 3) {
-        int cum = 0, b = 0;
-        for (; b < kLBins - 1; ++b) {
-          cum += hist[b * kLThreads + tid];
-          if (cum >= K) break;
-        }
-        if (b >= kLBins - 1 || cum > KC) path = 4;  // a dense bin, or the K-th value far below the maximum
-        bcut = b;
-      }
+      if (path == 2) path = over <= KC ? 1 : 4;
     }
     uint32_t pre = 0;
     int need = K;
     if (__any_sync(kFull, path == 4)) {
+      uint8_t* h8 = reinterpret_cast<uint8_t*>(stages);  // [digit][thread] (the bin histograms are no longer read)
       uint32_t pmask = 0;
 #pragma unroll 1
       for (int shf = 24; shf >= 0; shf -= 8) {
         if (path == 4)
-          for (int b = 0; b < 256; ++b) hist[b * kLThreads + tid] = 0;
+          for (int b = 0; b < 256; ++b) h8[b * kLThreads + tid] = 0;
 #pragma unroll 1
         for (int c = 0; c < nch; ++c) {
           float v[32];
@@ -479,14 +546,14 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const uint32_t ok = ordkey(v[j]);
-              if (v[j] > -INFINITY && (ok & pmask) == pre) hist[((ok >> shf) & 255u) * kLThreads + tid] += 1;
+              if (v[j] > -INFINITY && (ok & pmask) == pre) h8[((ok >> shf) & 255u) * kLThreads + tid] += 1;
             }
           }
         }
         if (path == 4) {
           int cum = 0, b = 255;
           for (; b > 0; --b) {
-            const int h = hist[b * kLThreads + tid];
+            const int h = h8[b * kLThreads + tid];
             if (cum + h >= need) break;
             cum += h;
           }
@@ -496,47 +563,10 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
         }
       }
     }
-    // the half's own bound (paths 3 and 4): at least K keys of the half are
-    // at or above it -- the smallest key within bin bcut, or the K-th key
-    uint64_t own = 0;
-    if (__any_sync(kFull, path >= 3)) {
-      uint64_t kmin = ~0ull;
-      int ties = 0;
-#pragma unroll 1
-      for (int c = 0; c < nch; ++c) {
-        float v[32];
-        chunk(c, v);
-        if (path >= 3) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const uint64_t k = rankkey(v[j], id0 + (uint32_t)(c * 32 + j));
-            const bool fin = v[j] > -INFINITY;
-            if (path == 3 && fin && value_bin(v[j], mh) <= bcut) kmin = k < kmin ? k : kmin;
-            if (path == 4 && fin && (uint32_t)(k >> 32) == pre && ++ties == need) own = k;
-          }
-        }
-      }
-      if (path == 3) own = kmin;
-    }
-    // the tile's bound: the largest of its eight halves' bounds (exchanged
-    // through the free part of the stage buffers, which every CTA of the
-    // cluster has stopped loading into), and the row's shared threshold
-    uint64_t* xb = reinterpret_cast<uint64_t*>(stages + 65536);  // [rank * 2 + half][row]
-#pragma unroll
-    for (uint32_t q = 0; q < (uint32_t)kLCluster; ++q)
-      st_cluster_u64(cluster_addr(&xb[(rank * 2 + half) * kLM + r_local], q), own);
-    cluster_sync_all();
-    uint64_t cb = 0;
-#pragma unroll
-    for (int i = 0; i < 2 * kLCluster; ++i) cb = xb[i * kLM + r_local] > cb ? xb[i * kLM + r_local] : cb;
     if (__any_sync(kFull, path != 0)) {
-      uint64_t teff = cb > tau ? cb : tau;
-      if (candrow) {
-        const uint64_t rt = ld_cg(&a.row_tau[row]);
-        teff = rt > teff ? rt : teff;
-      }
       uint64_t* dst = a.cand + (row * a.max_parts + part) * (int64_t)KC;
-      int cnt = 0;
+      int cnt = 0, ties = 0;
+      uint64_t theta = 0;
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
         float v[32];
@@ -545,15 +575,25 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const uint64_t k = rankkey(v[j], id0 + (uint32_t)(c * 32 + j));
-            // at most KC keys: teff is at or above the bound this half's path guarantees
-            if (v[j] > -INFINITY && k >= teff && cnt < KC) dst[cnt++] = k;
+            const uint32_t ok = (uint32_t)(k >> 32);
+            const bool fin = v[j] > -INFINITY;
+            bool take = fin && k >= teff;
+            if (path == 4) {
+              const bool tie = fin && ok == pre;
+              const bool top = fin && (ok > pre || (tie && ties < need));
+              if (tie && top && ++ties == need) theta = k;
+              take = take && top;
+            }
+            if (take && cnt < KC) dst[cnt++] = k;
           }
         }
       }
-      if (path != 0) a.cand_n[row * a.max_parts + part] = cnt | (cnt < nfin ? (1 << 30) : 0);
+      if (path != 0) {
+        a.cand_n[row * a.max_parts + part] = cnt | (cnt < nfin ? (1 << 30) : 0);
+        if (path == 4 && theta > teff)
+          atomicMax(reinterpret_cast<unsigned long long*>(&a.row_tau[row]), (unsigned long long)theta);
+      }
     }
-    if (candrow && rank == 0 && half == 0 && cb)
-      atomicMax(reinterpret_cast<unsigned long long*>(&a.row_tau[row]), (unsigned long long)cb);
     if (vrow && bad) atomicOr(&a.status[row], kStatusNonFinite);
   }
 
