@@ -195,19 +195,18 @@ constexpr uint32_t lm_idesc() {
 
 namespace pm {
 
-// Edges of the candidate histogram below the tile maximum m: e_b = fl(m -
-// (b + 1) / 4), non-increasing in b.  Bin b holds e_b <= x < e_{b-1}; the
-// last bin everything below e_62.
-__device__ __forceinline__ float tile_edge(float m, int b) { return fsub(m, 0.25f * (float)(b + 1)); }
-
-__device__ __forceinline__ int tile_bin(float x, float m) {
-  const float d = fmul(fsub(m, x), 4.0f);
-  int b = d < (float)(kLBins - 1) ? (int)d : kLBins - 1;
-  // settle the estimate on the edges (usually no step): afterwards
-  // bin(x) <= b exactly when x >= e_b, for every b < 63
-  while (b < kLBins - 1 && x < tile_edge(m, b)) ++b;
-  while (b > 0 && x >= tile_edge(m, b - 1)) --b;
-  return b;
+// Quarter-unit cells of the value axis: qcell(x) = floor(4 x), exact (4 x is
+// exact in fp32), clamped to +-2^22 so that every cell edge c / 4 is an exact
+// fp32 value.  x >= c / 4 exactly when qcell(x) >= c (for c > -2^22).  The
+// candidate histograms count values by cell below the tile maximum's cell.
+constexpr int kCellLim = 1 << 22;
+__device__ __forceinline__ int qcell(float x) {
+  return (int)floorf(fminf(fmaxf(fmul(x, 4.0f), -(float)kCellLim), (float)kCellLim));
+}
+__device__ __forceinline__ float cell_edge(int c) { return (float)c * 0.25f; }
+__device__ __forceinline__ int cell_bin(float x, int cm) {
+  const int b = cm - qcell(x);
+  return b < kLBins - 1 ? b : kLBins - 1;
 }
 
 struct LmParams {
@@ -217,6 +216,11 @@ struct LmParams {
   int32_t n_groups;      // row groups of 128
   float* logits;         // plain mode: [n_tok, logits_stride] fp32 out
   int64_t logits_stride;
+  // fused mode, zeroed before the launch: each row's histogram of candidate
+  // values by quarter-unit cell below its reference cell, and that cell
+  // (+ 2^22 + 1; 0: not set yet)
+  uint32_t* row_hist;    // [n_tok, 64]
+  uint32_t* row_cell;    // [n_tok]
 };
 
 // One CTA: rows [g 128, g 128 + 128) x ids [v0, v0 + 256), v0 = tile 1024 +
@@ -400,6 +404,7 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
       const uint64_t rt = ld_cg(&a.row_tau[row]);
       bfloor = rt ? key_value(rt) : -INFINITY;
     }
+    const int cm = m > -INFINITY ? qcell(m) : 0;  // the tile maximum's cell
     if (binned)
       for (int b4 = 0; b4 < kLBins / 4; ++b4) hist[b4 * kLThreads + tid] = 0;
     uint64_t s = 0;
@@ -419,7 +424,7 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           if (v[j] > -INFINITY && v[j] >= bfloor) {
-            const int b = tile_bin(v[j], m);
+            const int b = cell_bin(v[j], cm);
             hist[(b >> 2) * kLThreads + tid] += 1u << ((b & 3) * 8);
           }
       }
@@ -433,12 +438,18 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
     for (int b4 = 0; b4 < kLBins / 4; ++b4)
       st_cluster_u32(cluster_addr(&hx[(hi * (kLBins / 4) + b4) * kLM + r_local], 0), binned ? hist[b4 * kLThreads + tid] : 0u);
     cluster_sync_all();
-    // rank 0: the tile's statistics, and its bound for filtered rows -- the
-    // edge of the first bin where the tile's count reaches K (a synthetic key,
-    // low bits 0: at least K keys of the tile lie at or above it), sent to
-    // every CTA of the cluster and raised into the row's shared threshold
-    uint64_t* tb = reinterpret_cast<uint64_t*>(stages + 16384 + 65536);  // [row]: tile bound
-    int32_t* bs = reinterpret_cast<int32_t*>(tb + kLM);                   // [row]: its bin
+    // rank 0, per row: the tile's statistics; for filtered rows the tile's
+    // histogram (the eight halves summed) goes into the row's global
+    // histogram, whose cells are counted from the cell of the first tile that
+    // reached the row (so every tile adds by an integer shift); the bound is
+    // the higher of two lower edges -- of the first cell where the tile's own
+    // count reaches K and of the first where the row's count so far does --
+    // as a synthetic key (low bits 0: at least K keys lie at or above it),
+    // raised into the row's shared threshold and sent to every CTA of the
+    // cluster with its bin in this tile (bl: the halves' count there bounds
+    // what they emit)
+    uint64_t* tb = reinterpret_cast<uint64_t*>(stages + 16384 + 65536);  // [row]: the bound
+    int32_t* bs = reinterpret_cast<int32_t*>(tb + kLM);                   // [row]: its bin in this tile
     if (rank == 0 && half == 0) {
       if (vrow) {
         uint64_t tot = 0;
@@ -451,10 +462,14 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
         a.statx[row * a.n_tiles + tile] = t;
       }
       uint64_t tkey = 0;
-      int bstar = kLBins;
-      if (candrow) {
-        int cum = 0;
-        for (int b4 = 0; b4 < kLBins / 4 && bstar == kLBins; ++b4) {
+      int bl = kLBins;  // none
+      if (candrow && m > -INFINITY) {
+        uint32_t* gh = lp.row_hist + row * kLBins;
+        unsigned cr = atomicCAS(lp.row_cell + row, 0u, (unsigned)(cm + kCellLim + 1));
+        const int cref = cr ? (int)cr - kCellLim - 1 : cm;  // the row's reference cell
+        const int shift = cref - cm;                         // tile bin b is row bin b + shift
+        int cum = 0, bt = kLBins;
+        for (int b4 = 0; b4 < kLBins / 4; ++b4) {
           uint32_t lo = 0, hi2 = 0;  // bins b4*4 + {0, 2} and {1, 3} in 16-bit lanes
 #pragma unroll
           for (int q = 0; q < 2 * kLCluster; ++q) {
@@ -466,34 +481,48 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int b = b4 * 4 + e;
-            if (bstar == kLBins && b < kLBins - 1) {
-              cum += cnt4[e];
-              if (cum >= K) bstar = b;
+            if (b < kLBins - 1 && cnt4[e]) {
+              if (bt == kLBins) {
+                cum += cnt4[e];
+                if (cum >= K) bt = b;
+              }
+              const int gb = b + shift;
+              if (gb < kLBins - 1) atomicAdd(gh + (gb > 0 ? gb : 0), (unsigned)cnt4[e]);
             }
           }
         }
-        if (bstar < kLBins - 1) {
-          tkey = (uint64_t)ordkey(tile_edge(m, bstar)) << 32;
+        int bc = bt < kLBins - 1 ? cm - bt : -kCellLim;  // the bound's cell
+        int gcum = 0;
+        for (int gb = 0; gb < kLBins - 1; ++gb) {
+          gcum += (int)ld_cg(gh + gb);
+          if (gcum >= K) {
+            bc = cref - gb > bc ? cref - gb : bc;
+            break;
+          }
+        }
+        if (bc > -kCellLim + 1) {
+          tkey = (uint64_t)ordkey(cell_edge(bc)) << 32;
           atomicMax(reinterpret_cast<unsigned long long*>(&a.row_tau[row]), (unsigned long long)tkey);
+          bl = cm - bc;  // < 0: no value of this tile reaches it
         }
       }
 #pragma unroll
       for (uint32_t q = 0; q < (uint32_t)kLCluster; ++q) {
         st_cluster_u64(cluster_addr(&tb[r_local], q), tkey);
-        st_cluster_u32(cluster_addr(&bs[r_local], q), (uint32_t)bstar);
+        st_cluster_u32(cluster_addr(&bs[r_local], q), (uint32_t)bl);
       }
     }
     cluster_sync_all();
     if (vrow && mode == kGreedy) a.best[row * a.max_parts + part] = bk;
 
     // candidates of filtered rows, one list per half slice (a row part): the
-    // keys at or above teff = max(tile bound, row threshold); at most KC of
-    // them when every finite key fits, or when the half's count within the
-    // tile bound fits; else a threshold the half proves itself -- the row's
+    // keys at or above teff = max(bound, row threshold); at most KC of them
+    // when every finite key fits, or when the half's count at or above the
+    // bound fits; else a threshold the half proves itself -- the row's
     // threshold when the keys above it fit, or exactly the half's top K by a
     // radix select over its keys
     const uint64_t tkey = tb[r_local];
-    const int bstar = bs[r_local];
+    const int bl = (int)bs[r_local];
     uint64_t teff = 0;
     int path = 0;  // 1 keys >= teff fit; 2 count the keys >= teff first; 4 the half's own top K
     if (candrow) {
@@ -501,12 +530,14 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
       teff = tkey > rt ? tkey : rt;
       if (nfin <= KC) {
         path = 1;
-      } else if (tkey) {
-        int le = 0;  // the half's values at or above the tile bound
-        for (int b4 = 0; b4 <= bstar / 4; ++b4) {
-          const uint32_t w = hist[b4 * kLThreads + tid];
+      } else if (tkey && bl <= kLBins - 2) {
+        int le = 0;  // the half's binned values at or above the bound (all it may emit)
+        if (bl >= 0) {
+          for (int b4 = 0; b4 <= bl / 4; ++b4) {
+            const uint32_t w = hist[b4 * kLThreads + tid];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) le += (b4 * 4 + e <= bstar) ? (int)((w >> (8 * e)) & 255u) : 0;
+            for (int e = 0; e < 4; ++e) le += (b4 * 4 + e <= bl) ? (int)((w >> (8 * e)) & 255u) : 0;
+          }
         }
         path = le <= KC ? 1 : (teff > tkey ? 2 : 4);
       } else {
@@ -564,6 +595,8 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
       }
     }
     if (__any_sync(kFull, path != 0)) {
+      // path 4 also needs every value at or above its K-th to count ties
+      const float tv = (path == 4 || !teff) ? -INFINITY : key_value(teff);
       uint64_t* dst = a.cand + (row * a.max_parts + part) * (int64_t)KC;
       int cnt = 0, ties = 0;
       uint64_t theta = 0;
@@ -574,10 +607,11 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
         if (path != 0) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
+            const bool fin = v[j] > -INFINITY;
+            if (!(fin && v[j] >= tv)) continue;  // below the threshold's value: never taken
             const uint64_t k = rankkey(v[j], id0 + (uint32_t)(c * 32 + j));
             const uint32_t ok = (uint32_t)(k >> 32);
-            const bool fin = v[j] > -INFINITY;
-            bool take = fin && k >= teff;
+            bool take = k >= teff;
             if (path == 4) {
               const bool tie = fin && ok == pre;
               const bool top = fin && (ok > pre || (tie && ties < need));
@@ -700,7 +734,8 @@ pm::LmParams lm_params(const pm_lmhead* h, int64_t vocab) {
 // Workspace of the fused call.
 struct LmLayout {
   int n_tiles = 0, KC = 0, max_parts = 0;
-  size_t status = 0, row_tau = 0, statx = 0, cand = 0, cand_n = 0, best = 0, row_lse = 0, total = 0;
+  size_t status = 0, row_tau = 0, row_hist = 0, row_cell = 0, statx = 0, cand = 0, cand_n = 0, best = 0, row_lse = 0,
+         total = 0;
 };
 
 size_t align256(size_t o) { return (o + 255) & ~(size_t)255; }
@@ -723,6 +758,8 @@ int plan_lm(const pm_lmhead* h, const pm_rows* r, LmLayout* L) {
   auto take = [&](size_t bytes) { o = align256(o); const size_t at = o; o += bytes; return at; };
   L->status = take(sizeof(int32_t) * R);
   L->row_tau = take(sizeof(uint64_t) * R);
+  L->row_hist = take(sizeof(uint32_t) * R * pm::kLBins);
+  L->row_cell = take(sizeof(uint32_t) * R);
   L->statx = take(sizeof(pm::TileStat) * R * L->n_tiles);
   L->cand = take(sizeof(uint64_t) * R * L->max_parts * L->KC);
   L->cand_n = take(sizeof(int32_t) * R * L->max_parts);
@@ -809,11 +846,13 @@ int pm_lmhead_sample(const pm_lmhead* h, const pm_rows* rows, const pm_noise* no
   a.max_parts = L.max_parts;
   a.fixed_parts = L.max_parts;
   a.n_warps = rows->rows * (int64_t)L.n_tiles;
-  // row status and shared thresholds start at zero
-  cudaError_t e = cudaMemsetAsync(a.status, 0, sizeof(int32_t) * rows->rows, st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(a.row_tau, 0, sizeof(uint64_t) * rows->rows, st);
+  // row status, shared thresholds and the rows' candidate histograms start
+  // at zero (the plan lays them out one after the other: one memset)
+  cudaError_t e = cudaMemsetAsync(ws + L.status, 0, L.statx - L.status, st);
   if (e != cudaSuccess) return cuda_fail(e);
-  const pm::LmParams lp = lm_params(h, rows->vocab);
+  pm::LmParams lp = lm_params(h, rows->vocab);
+  lp.row_hist = reinterpret_cast<uint32_t*>(ws + L.row_hist);
+  lp.row_cell = reinterpret_cast<uint32_t*>(ws + L.row_cell);
   rc = L.KC == 64 ? launch_lmhead<true, 64>(h, rows->vocab, a, lp, st) : launch_lmhead<true, 256>(h, rows->vocab, a, lp, st);
   if (rc) return rc;
   return pm_launch_merges(L.KC, a, st);
