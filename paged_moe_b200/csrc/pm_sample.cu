@@ -808,6 +808,70 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
     const int K = (p.top_k > 0 && p.top_k < KC) ? p.top_k : KC;
     const bool needx = needs_xstats(a, p, mode);
     const bool needa = needs_astats(a, p, mode);
+    // Rows of many short part lists (the fused LM-head pass: one part per
+    // 128 ids): every count in one load per thread, a block scan, every key
+    // copied into the fold buffers, one block radix select of the top K.
+    // Keys below the row's shared bound may come along; they cannot reach
+    // the top K, since at least K listed keys lie at or above it.  Longer
+    // lists fall back to the per-warp fold below.
+    int ncarry = 0;
+    bool dropped = false;
+    bool gathered = false;
+    if (a.fixed_parts > 0) {
+      uint64_t* U = &mc->cand[0][0];
+      constexpr int kUcap = 8 * CAP;
+      if (wid == 0) {
+        if (needx) {
+          float mx;
+          const float c = warp_combine(a.statx + row * a.n_tiles, a.n_tiles, &mx);
+          if (lane == 0) mc->lse = c;
+        }
+      } else {
+        // warps 1..7: part q = (wid - 1) * 32 + lane + 224 i
+        int mine = 0;
+        bool trim = false;
+        for (int q = tid - 32; q < n_parts; q += 224) {
+          const int raw = ld_cg(&a.cand_n[row * a.max_parts + q]);
+          mine += raw & 0x3fffffff;
+          trim |= ((raw >> 30) & 1) != 0;
+        }
+        const int incl = warp_incl_scan(mine);
+        if (lane == 31) mc->wcnt[wid] = incl;
+        const bool wt = __any_sync(kFull, trim) != 0;
+        if (lane == 0) mc->wtrim[wid] = wt;
+        mine = incl - mine;  // this thread's offset within its warp
+        // stash the offset in the carry's score slots until the scan is done
+        reinterpret_cast<int*>(mc->u)[tid] = mine;
+      }
+      __syncthreads();
+      int tot = 0;
+      int wbase[8];
+#pragma unroll
+      for (int w = 1; w < 8; ++w) {
+        wbase[w] = tot;
+        tot += mc->wcnt[w];
+      }
+      bool trim_any = false;
+#pragma unroll
+      for (int w = 1; w < 8; ++w) trim_any |= mc->wtrim[w] != 0;
+      gathered = tot <= kUcap;
+      if (gathered) {
+        if (wid > 0) {
+          int o = wbase[wid] + reinterpret_cast<int*>(mc->u)[tid];
+          for (int q = tid - 32; q < n_parts; q += 224) {
+            const int n = ld_cg(&a.cand_n[row * a.max_parts + q]) & 0x3fffffff;
+            const uint64_t* src = a.cand + (row * a.max_parts + q) * (int64_t)KC;
+            for (int i = 0; i < n; ++i) U[o + i] = ld_cg(&src[i]);
+            o += n;
+          }
+        }
+        __syncthreads();
+        ncarry = block_topk_sorted(U, tot, K, mc->carry, KC, mc->mhist, mc->scal);
+        dropped = trim_any || tot > K;
+        __syncthreads();
+      }
+    }
+    if (!gathered) {
     // 1. warp 0: the row log-sum-exp (or its bracket).  Warps 1..7 (fw = wid - 1): parts fw,
     //    fw + 7, ... into their own top-K, from the row's shared threshold; a
     //    round takes 32 of the warp's parts at once (lane i: part
@@ -875,7 +939,7 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
     __syncthreads();
     // 2. the eight lists end to end, then the row's top-K sorted into the carry
     int tot = 0, start[8];
-    bool dropped = false;
+    dropped = false;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       start[w] = tot;
@@ -891,7 +955,6 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
       if (tid < mc->wcnt[w]) mc->u[start[w] + tid] = mine[w];
     __syncthreads();
     dropped |= tot > K;
-    int ncarry;
     if (tot <= 512) {
       // few keys: rank each by counting the larger ones (unique keys), the K
       // largest land sorted in the carry
@@ -907,6 +970,7 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
       ncarry = block_topk_sorted(mc->u, tot, K, mc->carry, KC, mc->mhist, mc->scal);
     }
     __syncthreads();
+    }
     // 3. the Gumbel scores of the row's top-K
     for (int r = tid; r < ncarry; r += 256)
       mc->score[r] = fadd(fmul(key_value(mc->carry[r]), p.inv_temperature), row_gumbel(a, row, key_index(mc->carry[r])));
