@@ -755,7 +755,8 @@ def run_lmhead(args):
         "gemm_only_graph_us": t_gemm,
         "cublas_bf16_gemm_graph_us": t_cublas,
         "roofline": {"bound": "tensor", "achieved": ach, "peak": tpk, "unit": "TFLOP/s", "frac": ach / tpk,
-                     "traffic": None, "peak_source": f"{kind} MEASURED_PEAKS.json bf16_tflops_sustained",
+                     "traffic": traffic_per_launch("k_lmhead", "lmhead"),
+                     "peak_source": f"{kind} MEASURED_PEAKS.json bf16_tflops_sustained",
                      "algorithmic_flops_per_launch": flops, "timing": "graph replay"},
         "clocks": clk.summary(),
     }
