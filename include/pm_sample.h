@@ -210,7 +210,9 @@ PM_API int pm_verify(const pm_rows *rows, const pm_noise *noise, const pm_verify
  * all-gather of pm_shard_summary_bytes per shard), and pm_shard_merge gives
  * every rank the row's tokens -- the same tokens, log-sum-exp and survivor
  * lists pm_sample_rows gives on the unsharded rows.  Rows whose unbounded
- * top-p / min-p keeps more than 256 tokens are flagged (status 1, token -1). */
+ * top-p / min-p keeps more than 256 tokens are flagged (status 1, token -1):
+ * the caller finishes them with pm_sample_rows on their whole rows (the
+ * Python layer all-gathers the flagged rows' slices for that). */
 typedef struct pm_shard {
     int32_t shard_index;
     int32_t n_shards;

@@ -155,6 +155,79 @@ def gather_summaries(summary: torch.Tensor, group=None) -> torch.Tensor:
     return torch.cat(parts)
 
 
+def _rows_of(x, idx, per_row_dim: int):
+    """Rows idx of a per-row argument: a tensor of per_row_dim dimensions
+    (fewer: shared by every row), or a sequence of per-row settings."""
+    if x is None:
+        return None
+    if isinstance(x, torch.Tensor):
+        return x[idx.to(x.device)] if x.dim() == per_row_dim else x
+    if isinstance(x, (list, tuple)):
+        return [x[int(i)] for i in idx.tolist()]
+    return x
+
+
+def _finish_wide(res: dict, full_rows, n_rows: int, sampler, processors, history, history_len, mask, seed: int,
+                 offset: int, row_base: int, gumbel, uniform, merge_kw: dict) -> dict:
+    """Rows the records cannot finish (status bit 1: an unbounded top-p /
+    min-p keeps more tokens than the candidate lists hold) get the unsharded
+    pass on their whole rows: the same kernels, so the same tokens, log-sum-
+    exp and status bits as sampling the unsharded rows.  full_rows(idx) gives
+    those rows' [len(idx), V] logits (an all-gather of the flagged rows'
+    slices on a process group).  Philox rows keep their own row ids."""
+    from . import engine
+    st = res.get("status")
+    if st is None:
+        return res
+    idx = torch.nonzero(st[:n_rows] & 1).flatten()
+    if idx.numel() == 0:
+        return res
+    rows = full_rows(idx)
+    for j, r in enumerate(idx.tolist()):
+        one = idx[j:j + 1]
+        hl = history_len
+        if hl is not None and not isinstance(hl, torch.Tensor):
+            hl = torch.as_tensor(hl, dtype=torch.int32)
+        sub = engine.sample_rows(
+            rows[j:j + 1], _rows_of(sampler, one, 0), _rows_of(processors, one, 0),
+            history=_rows_of(history, one, 2), history_len=_rows_of(hl, one, 1), mask=_rows_of(mask, one, 2),
+            seed=seed, offset=offset, row_base=row_base + r, gumbel=_rows_of(gumbel, one, 2),
+            uniform=_rows_of(uniform, one, 2),
+            return_lse=bool(merge_kw.get("return_lse")), return_logprob=bool(merge_kw.get("return_logprob")),
+            survivors=int(merge_kw.get("survivors") or 0), return_status=True)
+        res["tokens"][r] = sub["tokens"][0]
+        res["status"][r] = sub["status"][0]
+        for k in ("lse", "logprob", "n_surv"):
+            if k in res and k in sub:
+                res[k][r] = sub[k][0]
+        for k in ("surv_ids", "surv_probs"):
+            if k in res and k in sub:
+                res[k][r] = sub[k][0]
+    return res
+
+
+def gather_rows(logits_shard: torch.Tensor, idx: torch.Tensor, spec: ShardSpec, group=None) -> torch.Tensor:
+    """Rows idx of the full [B, V] logits on every rank: each rank's slice of
+    those rows (padded to the shard width), one all-gather, the slices end to
+    end."""
+    import torch.distributed as dist
+    n = dist.get_world_size(group)
+    part = torch.zeros((idx.numel(), spec.width), dtype=logits_shard.dtype, device=logits_shard.device)
+    part[:, : spec.hi - spec.lo] = logits_shard[idx.to(logits_shard.device)]
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty((n,) + tuple(part.shape), dtype=part.dtype, device=part.device)
+        dist.all_gather_into_tensor(out, part, group=group)
+        parts = list(out.unbind(0))
+    else:
+        parts = [torch.empty_like(part) for _ in range(n)]
+        dist.all_gather(parts, part, group=group)
+    cols = []
+    for i, p_ in enumerate(parts):
+        sp = ShardSpec.of(i, n, spec.vocab_total)
+        cols.append(p_[:, : sp.hi - sp.lo])
+    return torch.cat(cols, dim=1).contiguous()
+
+
 def sample_vocab_sharded(logits_shard: torch.Tensor, sampler=None, processors=None, group=None, history=None,
                          history_len=None, mask=None, seed: int = 0, offset: int = 0, row_base: int = 0,
                          gumbel=None, uniform=None, vocab_total: Optional[int] = None, **merge_kw):
@@ -169,8 +242,15 @@ def sample_vocab_sharded(logits_shard: torch.Tensor, sampler=None, processors=No
     s = summarize(logits_shard, spec, sampler, processors, history, history_len, mask, seed, offset, row_base,
                   gumbel, uniform)
     allsum = gather_summaries(s, group)
-    return merge(allsum, spec, logits_shard.shape[0], sampler, processors, seed, offset, row_base, gumbel,
-                 uniform, **merge_kw)
+    want_status = bool(merge_kw.pop("return_status", False))
+    B = logits_shard.shape[0]
+    res = merge(allsum, spec, B, sampler, processors, seed, offset, row_base, gumbel, uniform, return_status=True,
+                **merge_kw)
+    res = _finish_wide(res, lambda idx: gather_rows(logits_shard, idx, spec, group), B, sampler, processors,
+                       history, history_len, mask, seed, offset, row_base, gumbel, uniform, merge_kw)
+    if not want_status:
+        res.pop("status", None)
+    return res
 
 
 def emulate(logits: torch.Tensor, n_shards: int, sampler=None, processors=None, history=None, history_len=None,
@@ -184,5 +264,12 @@ def emulate(logits: torch.Tensor, n_shards: int, sampler=None, processors=None, 
         parts.append(summarize(logits[:, spec.lo:spec.hi], spec, sampler, processors, history, history_len, mask,
                                seed, offset, row_base, gumbel, uniform))
     spec0 = ShardSpec.of(0, n_shards, V)
-    return merge(torch.cat(parts), spec0, logits.shape[0], sampler, processors, seed, offset, row_base, gumbel,
-                 uniform, **merge_kw)
+    want_status = bool(merge_kw.pop("return_status", False))
+    B = logits.shape[0]
+    res = merge(torch.cat(parts), spec0, B, sampler, processors, seed, offset, row_base, gumbel, uniform,
+                return_status=True, **merge_kw)
+    res = _finish_wide(res, lambda idx: logits[idx.to(logits.device)], B, sampler, processors, history, history_len,
+                       mask, seed, offset, row_base, gumbel, uniform, merge_kw)
+    if not want_status:
+        res.pop("status", None)
+    return res

@@ -101,3 +101,27 @@ def test_sharded_exchange_two_gloo_ranks():
     with tempfile.TemporaryDirectory() as d:
         mp.start_processes(_worker, args=(_free_port(), d), nprocs=N, start_method="spawn", join=True)
         assert all(os.path.exists(os.path.join(d, f"ok{r}")) for r in range(N))
+
+
+def _gather_worker(rank, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=N)
+    try:
+        from paged_moe_b200 import shard as S
+        full = torch.arange(5 * 3000, dtype=torch.float32).reshape(5, 3000)
+        spec = S.ShardSpec.of(rank, N, 3000)
+        idx = torch.tensor([4, 1, 2])
+        got = S.gather_rows(full[:, spec.lo:spec.hi].contiguous(), idx, spec)
+        np.save(os.path.join(out_dir, f"g{rank}.npy"), got.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_rows_two_ranks():
+    # the whole rows of flagged rows, rebuilt from every rank's slice
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_gather_worker, args=(port, d), nprocs=N, join=True, start_method="spawn")
+        full = np.arange(5 * 3000, dtype=np.float32).reshape(5, 3000)
+        for r in range(N):
+            np.testing.assert_array_equal(np.load(os.path.join(d, f"g{r}.npy")), full[[4, 1, 2]])

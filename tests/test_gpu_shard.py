@@ -97,3 +97,22 @@ def test_shard_width_rule():
     assert S.shard_width(151936, 8) == 19456
     with pytest.raises(ValueError):
         S.shard_width(2048, 8)
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+@pytest.mark.parametrize("injected", [True, False])
+@pytest.mark.parametrize("s", [SamplerSettings(temp=1.0, top_p=0.9), SamplerSettings(temp=0.8, min_p=0.02),
+                               SamplerSettings(temp=1.0, top_p=0.5, min_p=0.01)])
+def test_unbounded_rows_beyond_the_records(n, injected, s):
+    # flat rows: an unbounded top-p / min-p keeps thousands of tokens, more
+    # than the records' candidates; those rows are finished on their
+    # gathered whole rows and must equal the unsharded pass bit for bit
+    rng = np.random.default_rng(70 + n)
+    B, V = 12, 65536
+    x = (rng.standard_normal((B, V)) * 0.5).astype(np.float32)
+    x[3] = W.peaked_logits(rng, 1, V, 2.0, 8.0, 4)[0]  # a peaked row the records do finish
+    sh, un, _, _ = _both(x, s, n, injected=injected)
+    np.testing.assert_array_equal(sh["tokens"], un["tokens"])
+    np.testing.assert_array_equal(sh["lse"].view(np.uint32), un["lse"].view(np.uint32))
+    np.testing.assert_array_equal(sh["status"], un["status"])
+    assert (sh["status"] & 1).sum() == 0
