@@ -167,8 +167,8 @@ def _rows_of(x, idx, per_row_dim: int):
     return x
 
 
-def _finish_wide(res: dict, full_rows, n_rows: int, sampler, processors, history, history_len, mask, seed: int,
-                 offset: int, row_base: int, gumbel, uniform, merge_kw: dict) -> dict:
+def _finish_wide(res: dict, full_rows, n_rows: int, vocab: int, sampler, processors, history, history_len, mask,
+                 seed: int, offset: int, row_base: int, gumbel, uniform, merge_kw: dict) -> dict:
     """Rows the records cannot finish (status bit 1: an unbounded top-p /
     min-p keeps more tokens than the candidate lists hold) get the unsharded
     pass on their whole rows: the same kernels, so the same tokens, log-sum-
@@ -178,6 +178,10 @@ def _finish_wide(res: dict, full_rows, n_rows: int, sampler, processors, history
     from . import engine
     st = res.get("status")
     if st is None:
+        return res
+    # only rows with an unbounded filter can be flagged: no host sync otherwise
+    _, flags_any, _, _, _, _ = _params_for(st.device, sampler, processors, n_rows, vocab)
+    if not (flags_any & L.PM_F_UNBOUNDED):
         return res
     idx = torch.nonzero(st[:n_rows] & 1).flatten()
     if idx.numel() == 0:
@@ -246,8 +250,8 @@ def sample_vocab_sharded(logits_shard: torch.Tensor, sampler=None, processors=No
     B = logits_shard.shape[0]
     res = merge(allsum, spec, B, sampler, processors, seed, offset, row_base, gumbel, uniform, return_status=True,
                 **merge_kw)
-    res = _finish_wide(res, lambda idx: gather_rows(logits_shard, idx, spec, group), B, sampler, processors,
-                       history, history_len, mask, seed, offset, row_base, gumbel, uniform, merge_kw)
+    res = _finish_wide(res, lambda idx: gather_rows(logits_shard, idx, spec, group), B, vocab_total, sampler,
+                       processors, history, history_len, mask, seed, offset, row_base, gumbel, uniform, merge_kw)
     if not want_status:
         res.pop("status", None)
     return res
@@ -268,8 +272,8 @@ def emulate(logits: torch.Tensor, n_shards: int, sampler=None, processors=None, 
     B = logits.shape[0]
     res = merge(torch.cat(parts), spec0, B, sampler, processors, seed, offset, row_base, gumbel, uniform,
                 return_status=True, **merge_kw)
-    res = _finish_wide(res, lambda idx: logits[idx.to(logits.device)], B, sampler, processors, history, history_len,
-                       mask, seed, offset, row_base, gumbel, uniform, merge_kw)
+    res = _finish_wide(res, lambda idx: logits[idx.to(logits.device)], B, V, sampler, processors, history,
+                       history_len, mask, seed, offset, row_base, gumbel, uniform, merge_kw)
     if not want_status:
         res.pop("status", None)
     return res
