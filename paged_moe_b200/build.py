@@ -56,10 +56,34 @@ def _stale() -> bool:
     return any(os.path.getmtime(d) > t for d in sources() + _headers() if os.path.exists(d))
 
 
+class _BuildLock:
+    """An exclusive lock on a file beside the library while a build runs:
+    processes that start together (ranks of one job, test workers) build
+    once, the others wait and then find the outputs fresh."""
+
+    def __enter__(self):
+        import fcntl
+        self.f = open(os.path.join(HERE, ".build.lock"), "a+")
+        fcntl.flock(self.f, fcntl.LOCK_EX)
+        return self
+
+    def __exit__(self, *exc):
+        import fcntl
+        fcntl.flock(self.f, fcntl.LOCK_UN)
+        self.f.close()
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     """Compile every translation unit (in parallel) and link the library."""
     if not force and not _stale():
         return SO
+    with _BuildLock():
+        if not force and not _stale():
+            return SO
+        return _build_locked(verbose)
+
+
+def _build_locked(verbose: bool) -> str:
     os.makedirs(OBJDIR, exist_ok=True)
     cc = nvcc()
     procs = []
@@ -67,7 +91,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     for src in sources():
         obj = os.path.join(OBJDIR, os.path.basename(src) + ".o")
         objs.append(obj)
-        cmd = [cc, *NVCC_FLAGS, "-c", "-o", obj + ".tmp", src]
+        cmd = [cc, *NVCC_FLAGS, "-c", "-o", obj + f".{os.getpid()}.tmp", src]
         if verbose:
             print(" ".join(cmd), flush=True)
         procs.append((obj, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)))
@@ -80,15 +104,16 @@ def build(force: bool = False, verbose: bool = False) -> str:
         else:
             if verbose and out:
                 sys.stderr.write(out)
-            os.replace(obj + ".tmp", obj)
+            os.replace(obj + f".{os.getpid()}.tmp", obj)
     if failed:
         raise RuntimeError("nvcc failed building libpm_sample.so")
-    cmd = [cc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", SO + ".tmp", *objs, "-lcudart"]
+    tmp = SO + f".{os.getpid()}.tmp"
+    cmd = [cc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs, "-lcudart"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)
         raise RuntimeError("linking libpm_sample.so failed")
-    os.replace(SO + ".tmp", SO)
+    os.replace(tmp, SO)
     return SO
 
 
@@ -103,11 +128,24 @@ def ext_path() -> str:
 def build_ext(force: bool = False, verbose: bool = False) -> str:
     """Compile the PyTorch extension module _pm_torch (pm_torch.cpp) against
     torch's headers, linked to libpm_sample.so beside it (rpath $ORIGIN)."""
-    import sysconfig
     out = ext_path()
-    deps = [EXT_SRC, os.path.join(ROOT, "include", "pm_sample.h"), SO]
-    if not force and os.path.exists(out) and all(os.path.getmtime(d) <= os.path.getmtime(out) for d in deps):
+    # the module links libpm_sample.so dynamically: only its own source and
+    # the C ABI's header make it stale
+    deps = [EXT_SRC, os.path.join(ROOT, "include", "pm_sample.h")]
+
+    def fresh():
+        return os.path.exists(out) and all(os.path.getmtime(d) <= os.path.getmtime(out) for d in deps)
+
+    if not force and fresh():
         return out
+    with _BuildLock():
+        if not force and fresh():
+            return out
+        return _build_ext_locked(out, verbose)
+
+
+def _build_ext_locked(out: str, verbose: bool) -> str:
+    import sysconfig
     cxx = os.environ.get("CXX", "g++")
     if not shutil.which(cxx):
         raise CompilerMissing(f"{cxx} not found")
@@ -119,7 +157,8 @@ def build_ext(force: bool = False, verbose: bool = False) -> str:
            f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_pm_torch", "-DTORCH_API_INCLUDE_EXTENSION_H",
            f"-I{sysconfig.get_paths()['include']}", f"-I{os.path.join(cuda_home, 'include')}"]
     cmd += [f"-I{p}" for p in ce.include_paths()]
-    cmd += ["-o", out + ".tmp", EXT_SRC]
+    tmp = out + f".{os.getpid()}.tmp"
+    cmd += ["-o", tmp, EXT_SRC]
     cmd += [f"-L{p}" for p in ce.library_paths()]
     cmd += [f"-L{HERE}", "-lpm_sample", "-Wl,-rpath,$ORIGIN",
             "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
@@ -130,7 +169,7 @@ def build_ext(force: bool = False, verbose: bool = False) -> str:
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)
         raise RuntimeError("building the _pm_torch extension failed")
-    os.replace(out + ".tmp", out)
+    os.replace(tmp, out)
     return out
 
 
