@@ -112,7 +112,7 @@ typedef struct pm_rows {
     const int32_t *feed;         /* [rows / feed_group, feed_group] or NULL */
     int32_t feed_group;          /* rows per request when feed != NULL */
     /* logit bias shared by all rows (mlx-lm logit_bias) */
-    const int32_t *bias_tokens;  /* [n_bias] distinct ids, ascending */
+    const int32_t *bias_tokens;  /* [n_bias] distinct ids, ascending (an id out of order is not applied) */
     const float *bias_values;    /* [n_bias] */
     int32_t n_bias;
     /* allowed-token bitmask: bit v of word v/32 of row r; NULL = all allowed */
@@ -283,10 +283,11 @@ PM_API int pm_lmhead_logits(const pm_lmhead *h, int64_t vocab, float *logits, in
  * pm_lmhead_logits computes (tokens, log-sum-exp, survivors, bit for bit).
  * rows: rows == h->n_tokens and rows->logits unused; greedy rows and rows
  * with 0 < top_k <= 256 (temperature, top_p and min_p on top), with the
- * allowed-token mask.  Penalties, logit bias, forced tokens, unbounded
- * top-p / min-p and whole-vocabulary draws return PM_ERR_UNSUPPORTED (use
- * pm_lmhead_logits + pm_sample_rows).  Row status bit 128: a logit was NaN or
- * +inf.  The workspace needs no zeroing. */
+ * processors (logit bias, repetition / presence / frequency penalties over
+ * rows->hist) and the allowed-token mask.  Verify feeds, forced tokens,
+ * unbounded top-p / min-p and whole-vocabulary draws return
+ * PM_ERR_UNSUPPORTED (use pm_lmhead_logits + pm_sample_rows).  Row status
+ * bit 128: a logit was NaN or +inf.  The workspace needs no zeroing. */
 PM_API size_t pm_lmhead_sample_workspace_bytes(const pm_lmhead *h, const pm_rows *rows);
 PM_API int pm_lmhead_sample(const pm_lmhead *h, const pm_rows *rows, const pm_noise *noise,
                             const pm_sample_out *out, void *workspace, size_t workspace_bytes, void *stream);

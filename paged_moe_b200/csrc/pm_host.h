@@ -88,6 +88,13 @@ struct SampleArgs;
 // whose logits can be fetched as aligned 4-byte words.
 int pm_launch_masked(int dtype, int KC, const pm::SampleArgs& a, cudaStream_t st);
 
+// The processors' device lists (penalty overrides by tile, logit-bias tile
+// offsets) for a pass of another translation unit (pm_lmhead.cu): bytes of
+// the region (0: a history window beyond the build's cap), and the prep
+// kernels that fill it and the processor fields of `a` (a.status must be set).
+size_t pm_prep_bytes(const pm_rows* r, int n_tiles);
+int pm_prep_launch(const pm_rows* r, int n_tiles, unsigned char* region, pm::SampleArgs& a, cudaStream_t st);
+
 // The row merges (pm_sample.cu) over parts that a pass of another
 // translation unit wrote (pm_lmhead.cu).
 int pm_launch_merges(int KC, const pm::SampleArgs& a, cudaStream_t st);

@@ -145,6 +145,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 consecutive fp32 columns back into this thread's TMEM lane (the
+// store is complete when this returns).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  __syncwarp();
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]),
+      "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]), "f"(v[18]),
+      "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]),
+      "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -194,6 +209,44 @@ constexpr uint32_t lm_idesc() {
 }  // namespace pm
 
 namespace pm {
+
+// The processors' entries of one 32-id chunk (ids c0id ..), in the order of
+// the other passes: logit bias, then the row's repetition, presence and
+// frequency overrides (the mask comes later, as the chunk is read).
+__device__ __forceinline__ void lm_processors(const SampleArgs& a, int64_t row, int64_t c0id, int ob, int oe, int bb,
+                                              int be, float (&v)[32]) {
+  for (int i = bb; i < be; ++i) {
+    const int64_t jj = a.bias_tok[i] - c0id;
+    if (jj >= 0 && jj < 32) {
+      const float bv = a.bias_val[i];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j == jj) v[j] = fadd(v[j], bv);
+    }
+  }
+  if (oe > ob) {
+    const pm_row_params& pp = row_params(a, row);
+    const int32_t* otok = a.ovr_tok + row * (int64_t)a.ovr_cap;
+    const uint32_t* oinf = a.ovr_info + row * (int64_t)a.ovr_cap;
+    for (int i = ob; i < oe; ++i) {
+      const int64_t jj = otok[i] - c0id;
+      if (jj >= 0 && jj < 32) {
+        const uint32_t info = oinf[i];
+        float x = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j == jj) x = v[j];
+        if (info & 1u) x = x < 0.0f ? fmul(x, pp.repetition_penalty) : __fdiv_rn(x, pp.repetition_penalty);
+        if (info & 2u) x = fsub(x, pp.presence_penalty);
+        const uint32_t cnt = info >> 8;
+        if (cnt) x = fsub(x, fmul(pp.frequency_penalty, (float)cnt));
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j == jj) v[j] = x;
+      }
+    }
+  }
+}
 
 // Quarter-unit cells of the value axis: qcell(x) = floor(4 x), exact (4 x is
 // exact in fp32), clamped to +-2^22 so that every cell edge c / 4 is an exact
@@ -341,6 +394,33 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
     // chunk c of the row's processed values: ids past the vocabulary and
     // disallowed ids (bit j of the row's mask word (id0 >> 5) + c) are -inf
     const uint32_t* mrow = (a.mask && vrow) ? a.mask + row * a.mask_stride + (id0 >> 5) : nullptr;
+    // the processors' entries of this tile: logit bias (shared by the rows)
+    // and the row's penalty overrides, applied to the chunk that holds them
+    // in the order of the other passes (bias, repetition, presence,
+    // frequency, then the mask)
+    int ob = 0, oe = 0, bb = 0, be = 0;
+    if (a.ovr_off && vrow) {
+      ob = a.ovr_off[row * (int64_t)(a.n_tiles + 1) + tile];
+      oe = a.ovr_off[row * (int64_t)(a.n_tiles + 1) + tile + 1];
+    }
+    if (a.bias_off) {
+      bb = a.bias_off[tile];
+      be = a.bias_off[tile + 1];
+    }
+    // once per tile, before the passes: the processed values replace the
+    // raw ones in TMEM (chunks of warps where some row has an entry)
+    {
+      const bool has = oe > ob || be > bb;
+      if (__any_sync(kFull, has)) {
+#pragma unroll 1
+        for (int c = 0; c < nch; ++c) {
+          float v[32];
+          tmem_ld32(tl + c * 32, v);
+          if (has) lm_processors(a, row, (int64_t)id0 + c * 32, ob, oe, bb, be, v);
+          tmem_st32(tl + c * 32, v);
+        }
+      }
+    }
     const bool plain = a.mask == nullptr;  // uniform: no mask words to apply
     auto chunk = [&](int c, float (&v)[32]) {
       const uint32_t w = mrow ? __ldg(mrow + c) : 0xFFFFFFFFu;
@@ -735,7 +815,7 @@ pm::LmParams lm_params(const pm_lmhead* h, int64_t vocab) {
 struct LmLayout {
   int n_tiles = 0, KC = 0, max_parts = 0;
   size_t status = 0, row_tau = 0, row_hist = 0, row_cell = 0, statx = 0, cand = 0, cand_n = 0, best = 0, row_lse = 0,
-         total = 0;
+         prep = 0, total = 0;
 };
 
 size_t align256(size_t o) { return (o + 255) & ~(size_t)255; }
@@ -746,8 +826,10 @@ int plan_lm(const pm_lmhead* h, const pm_rows* r, LmLayout* L) {
   // the fused pass finishes greedy rows and rows whose filters keep at most
   // top_k <= 256 tokens; processors other than the mask need the history
   // prep, and whole-vocabulary draws or unbounded filters need the row
-  if (r->hist || r->feed || r->n_bias > 0 || r->forced) return PM_ERR_UNSUPPORTED;
-  if (r->flags_any & (PM_F_UNBOUNDED | PM_F_FULL | PM_F_REP | PM_F_PRES | PM_F_FREQ)) return PM_ERR_UNSUPPORTED;
+  if (r->feed || r->forced) return PM_ERR_UNSUPPORTED;
+  if (r->flags_any & (PM_F_UNBOUNDED | PM_F_FULL)) return PM_ERR_UNSUPPORTED;
+  if (r->hist && r->hist_stride <= 0) return PM_ERR_ARG;
+  if (r->n_bias < 0 || (r->n_bias > 0 && (!r->bias_tokens || !r->bias_values))) return PM_ERR_ARG;
   if (r->top_k_max > 256) return PM_ERR_UNSUPPORTED;
   L->n_tiles = (int)((r->vocab + pm::kTile - 1) / pm::kTile);
   if (L->n_tiles > 32 * 8) return PM_ERR_UNSUPPORTED;  // the merge's log-sum-exp tree: 256 tiles at most
@@ -765,6 +847,9 @@ int plan_lm(const pm_lmhead* h, const pm_rows* r, LmLayout* L) {
   L->cand_n = take(sizeof(int32_t) * R * L->max_parts);
   L->best = take(sizeof(uint64_t) * R * L->max_parts);
   L->row_lse = take(sizeof(float) * R);
+  const size_t pb = pm_prep_bytes(r, L->n_tiles);
+  if (!pb) return PM_ERR_UNSUPPORTED;  // a penalty window beyond the build's history cap
+  L->prep = take(pb);
   L->total = align256(o);
   return PM_OK;
 }
@@ -850,6 +935,9 @@ int pm_lmhead_sample(const pm_lmhead* h, const pm_rows* rows, const pm_noise* no
   // at zero (the plan lays them out one after the other: one memset)
   cudaError_t e = cudaMemsetAsync(ws + L.status, 0, L.statx - L.status, st);
   if (e != cudaSuccess) return cuda_fail(e);
+  // the processors' lists: penalty overrides by tile, logit-bias offsets
+  rc = pm_prep_launch(rows, L.n_tiles, ws + L.prep, a, st);
+  if (rc) return rc;
   pm::LmParams lp = lm_params(h, rows->vocab);
   lp.row_hist = reinterpret_cast<uint32_t*>(ws + L.row_hist);
   lp.row_cell = reinterpret_cast<uint32_t*>(ws + L.row_cell);

@@ -145,6 +145,7 @@ __device__ __noinline__ void masked_overrides(const SampleArgs& a, const pm_row_
   const int lane = threadIdx.x & 31;
   const uint32_t t0 = (uint32_t)t * kTile;
   auto locate = [&](int id, bool in) -> int {  // list position of id, -1 if disallowed (all lanes call)
+    in = in && (uint32_t)id - t0 < (uint32_t)kTile;  // ids out of ascending order: skipped
     const uint32_t e = in ? (uint32_t)id - t0 : 0u;
     const uint32_t wj = __shfl_sync(kFull, word, (int)(e >> 5));
     const int pj = __shfl_sync(kFull, wpre, (int)(e >> 5));

@@ -1746,6 +1746,91 @@ int launch_accept(const pm::SampleArgs& a, int dtype, const pm::VerifyK& vk, int
 
 }  // namespace
 
+// The processors' device lists for a pass of another translation unit (the
+// fused LM-head pass): the penalty overrides bucketed by 1024-id tile and the
+// logit-bias tile offsets, laid out in `region` (pm_prep_bytes of it).
+size_t pm_prep_bytes(const pm_rows* r, int n_tiles) {
+  int cap = 0;
+  if (penalties_on(r)) {
+    const int64_t w = r->hist_stride + (r->feed ? r->feed_group : 0);
+    if (w > 8192) return 0;
+    cap = pow2_at_least(w < 32 ? 32 : w);
+  }
+  const int64_t R = r->rows;
+  return align_up(sizeof(int32_t) * R * cap, 256) + align_up(sizeof(uint32_t) * R * cap, 256) +
+         align_up(sizeof(int32_t) * R * (cap ? n_tiles + 1 : 0), 256) + align_up(sizeof(int32_t) * (n_tiles + 1), 256);
+}
+
+int pm_prep_launch(const pm_rows* r, int n_tiles, unsigned char* region, pm::SampleArgs& a, cudaStream_t st) {
+  Layout L;
+  L.n_tiles = n_tiles;
+  L.ovr_cap = 0;
+  if (penalties_on(r)) {
+    const int64_t w = r->hist_stride + (r->feed ? r->feed_group : 0);
+    if (w > 8192) return PM_ERR_UNSUPPORTED;
+    L.ovr_cap = pow2_at_least(w < 32 ? 32 : w);
+  }
+  const int64_t R = r->rows;
+  size_t o = 0;
+  L.ovr_tok = o;
+  o += align_up(sizeof(int32_t) * R * L.ovr_cap, 256);
+  L.ovr_info = o;
+  o += align_up(sizeof(uint32_t) * R * L.ovr_cap, 256);
+  L.ovr_off = o;
+  o += align_up(sizeof(int32_t) * R * (L.ovr_cap ? n_tiles + 1 : 0), 256);
+  L.bias_off = o;
+  a.ovr_tok = nullptr;
+  a.ovr_info = nullptr;
+  a.ovr_off = nullptr;
+  a.ovr_cap = L.ovr_cap;
+  a.bias_tok = nullptr;
+  a.bias_val = nullptr;
+  a.bias_off = nullptr;
+  cudaError_t e;
+  if (L.ovr_cap && R > 0) {
+    pm::PrepArgs pa;
+    pa.hist = r->hist;
+    pa.hist_len = r->hist_len;
+    pa.hist_stride = r->hist_stride;
+    pa.feed = r->feed;
+    pa.feed_group = r->feed_group;
+    pa.params = r->params;
+    pa.params_per_row = r->params_per_row;
+    pa.rows = R;
+    pa.vocab = r->vocab;
+    pa.id_base = 0;
+    pa.n_tiles = n_tiles;
+    pa.cap = L.ovr_cap;
+    pa.ovr_tok = reinterpret_cast<int32_t*>(region + L.ovr_tok);
+    pa.ovr_info = reinterpret_cast<uint32_t*>(region + L.ovr_info);
+    pa.ovr_off = reinterpret_cast<int32_t*>(region + L.ovr_off);
+    pa.status = a.status;
+    pa.row_tau = a.row_tau;
+    pa.exact_q = nullptr;
+    const size_t smem = sizeof(int) * (6 * (size_t)L.ovr_cap + 2 * 264);
+    static DeviceOnce once;
+    once([&] {
+      cudaFuncSetAttribute(pm::k_prep_overrides, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * (6 * 8192 + 2 * 264));
+    });
+    pm::k_prep_overrides<<<(unsigned)R, 1024, smem, st>>>(pa);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    a.ovr_tok = pa.ovr_tok;
+    a.ovr_info = pa.ovr_info;
+    a.ovr_off = pa.ovr_off;
+  }
+  if (r->n_bias > 0) {
+    a.bias_tok = r->bias_tokens;
+    a.bias_val = r->bias_values;
+    a.bias_off = reinterpret_cast<int32_t*>(region + L.bias_off);
+    pm::k_bias_offsets<<<(n_tiles + 256) / 256, 256, 0, st>>>(r->bias_tokens, r->n_bias, n_tiles,
+                                                               const_cast<int32_t*>(a.bias_off));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
+  return PM_OK;
+}
+
 // The row merges over parts written by another translation unit's pass (the
 // fused LM-head pass): rows never take the whole-vocabulary draw there, so
 // the logits type is immaterial.

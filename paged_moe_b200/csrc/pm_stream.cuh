@@ -101,8 +101,8 @@ __device__ __forceinline__ void apply_overrides_smem(const SampleArgs& a, const 
   const int lane = threadIdx.x & 31;
   const int64_t start = (int64_t)tile * kTile;
   for (int i = bb + lane; i < be; i += 32) {
-    const int e = (int)(a.bias_tok[i] - start);
-    buf[e] = fadd(buf[e], a.bias_val[i]);
+    const int64_t e = a.bias_tok[i] - start;
+    if (e >= 0 && e < kTile) buf[e] = fadd(buf[e], a.bias_val[i]);  // ids out of ascending order: skipped
   }
   __syncwarp();
   const int32_t* otok = a.ovr_tok + row * (int64_t)a.ovr_cap;

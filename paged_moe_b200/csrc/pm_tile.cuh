@@ -186,8 +186,8 @@ __device__ __forceinline__ void process_tile(const SampleArgs& a, const pm_row_p
     for (int s = 0; s < 32; ++s) wbuf[slot_elem<VW>(s, lane)] = ti.v[s];
     __syncwarp();
     for (int i = ti.bb + lane; i < ti.be; i += 32) {
-      const int e = (int)(a.bias_tok[i] - start);
-      wbuf[e] = fadd(wbuf[e], a.bias_val[i]);
+      const int64_t e = a.bias_tok[i] - start;
+      if (e >= 0 && e < kTile) wbuf[e] = fadd(wbuf[e], a.bias_val[i]);  // ids out of ascending order: skipped
     }
     __syncwarp();
     const int32_t* otok = a.ovr_tok + row * (int64_t)a.ovr_cap;

@@ -511,7 +511,9 @@ __device__ __forceinline__ void process_tile_regs(const SampleArgs& a, const pm_
   const int lane = threadIdx.x & 31;
   const int64_t start = (int64_t)tile * kTile;
   for (int i = ti.bb; i < ti.be; ++i) {
-    const int e = (int)(a.bias_tok[i] - start);
+    const int64_t e64 = a.bias_tok[i] - start;
+    if (e64 < 0 || e64 >= kTile) continue;  // ids out of ascending order: skipped
+    const int e = (int)e64;
     if ((e % (32 * VW)) / VW != lane) continue;
     const int sl = (e / (32 * VW)) * VW + e % VW;
     const float b = a.bias_val[i];

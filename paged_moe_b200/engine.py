@@ -396,14 +396,18 @@ def lmhead_logits(hidden: torch.Tensor, weight: torch.Tensor, out: Optional[torc
 
 def lmhead_sample(hidden: torch.Tensor, weight: torch.Tensor,
                   sampler: Union[SamplerSettings, Sequence[SamplerSettings]] = None,
+                  processors: Union[ProcessorSettings, Sequence[ProcessorSettings], None] = None,
+                  history: Optional[torch.Tensor] = None, history_len=None,
                   mask: Optional[torch.Tensor] = None, seed: int = 0, offset: int = 0, row_base: int = 0,
                   gumbel: Optional[torch.Tensor] = None, return_lse: bool = False, return_logprob: bool = False,
                   survivors: int = 0, return_status: bool = False):
     """The LM head fused with the sampler: the tokens (and the other outputs
     of sample_rows) that sample_rows would give on lmhead_logits(hidden,
     weight), with the logits never written to device memory.  Greedy rows and
-    rows with top_k (plus temperature, top_p, min_p) and an optional mask;
-    other settings raise (use lmhead_logits + sample_rows)."""
+    rows with top_k (plus temperature, top_p, min_p), the processors (logit
+    bias, repetition / presence / frequency penalties over `history`) and an
+    optional mask; unbounded top-p / min-p and whole-vocabulary draws raise
+    (use lmhead_logits + sample_rows)."""
     keep = _Keep()
     lib = L.load()
     s = _lmhead_struct(hidden, weight, keep)
@@ -411,7 +415,7 @@ def lmhead_sample(hidden: torch.Tensor, weight: torch.Tensor,
     B, V = hidden.shape[0], weight.shape[0]
     # the rows need a [B, V] logits view only for their shape: one row, broadcast
     stand_in = torch.empty((1, V), dtype=torch.float32, device=dev).expand(B, V)
-    r = build_rows(stand_in, sampler, None, None, None, mask, keep)
+    r = build_rows(stand_in, sampler, processors, history, history_len, mask, keep)
     r.logits = None
     n = _noise(B, V, seed, offset, row_base, gumbel, None, keep, dev)
     o = L.SampleOut()

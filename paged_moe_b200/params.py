@@ -61,6 +61,19 @@ class ProcessorSettings:
     frequency_penalty: Optional[float] = None
     frequency_context_size: int = 20
 
+    def __post_init__(self):
+        # the device lists are bucketed by token id: ascending, distinct ids
+        # (a dict, or pairs in any order, come out the same)
+        lb = self.logit_bias
+        if lb:
+            items = lb.items() if isinstance(lb, dict) else lb
+            norm = tuple(sorted((int(t), float(v)) for t, v in items))
+            if len({t for t, _ in norm}) != len(norm):
+                raise ValueError("logit_bias names a token more than once")
+            object.__setattr__(self, "logit_bias", norm)
+        elif lb is not None:
+            object.__setattr__(self, "logit_bias", None)
+
     @staticmethod
     def make(logit_bias: Optional[dict] = None, **kw) -> "ProcessorSettings":
         lb = tuple(sorted((int(k), float(v)) for k, v in logit_bias.items())) if logit_bias else None

@@ -192,3 +192,33 @@ def test_fused_ties_against_oracle(mode):
     for b in range(B):
         n = int(ref["n_surv"][b])
         np.testing.assert_array_equal(ids[b, :n], ref["surv_ids"][b, :n])
+
+
+def test_fused_with_processors():
+    # C1's settings (top_k 20, top_p 0.8, repetition over a 256-id window)
+    # plus presence, frequency and logit bias, per-row histories
+    from paged_moe_b200.params import ProcessorSettings
+    eng = _eng()
+    h, w = _operands(48, 512, 30000, seed=43)
+    rng = np.random.default_rng(44)
+    hist = torch.from_numpy(rng.integers(0, 30000, (48, 300)).astype(np.int32)).cuda()
+    hist[:, 100:140] = 7  # repeats: frequency counts above one
+    hl = torch.from_numpy(rng.integers(1, 301, 48).astype(np.int32)).cuda()
+    g = torch.from_numpy(W.gumbel(rng, (48, 30000))).cuda()
+    procs = [ProcessorSettings(repetition_penalty=1.05, repetition_context_size=256),
+             ProcessorSettings(repetition_penalty=1.3, repetition_context_size=64, presence_penalty=0.5,
+                               presence_context_size=100, frequency_penalty=0.2, frequency_context_size=300,
+                               logit_bias=((3, 4.0), (29999, 2.5), (1000, -3.0)))]
+    for p in procs:
+        for s in (SamplerSettings(temp=0.7, top_k=20, top_p=0.8), SamplerSettings(temp=0.0),
+                  SamplerSettings(temp=1.0, top_k=64, min_p=0.05)):
+            logits = eng.lmhead_logits(h, w)
+            ref = eng.sample_rows(logits, s, p, history=hist, history_len=hl, gumbel=g, return_lse=True,
+                                  return_status=True)
+            got = eng.lmhead_sample(h, w, s, p, history=hist, history_len=hl, gumbel=g, return_lse=True,
+                                    return_status=True)
+            torch.cuda.synchronize()
+            assert (got["status"].cpu() == 0).all(), got["status"]
+            np.testing.assert_array_equal(got["tokens"].cpu().numpy(), ref["tokens"].cpu().numpy())
+            np.testing.assert_array_equal(got["lse"].cpu().numpy().view(np.uint32),
+                                          ref["lse"].cpu().numpy().view(np.uint32))

@@ -93,3 +93,15 @@ def test_import_and_workloads_load_no_product_library():
                          cwd=__import__("os").path.dirname(__import__("os").path.dirname(__file__)))
     assert out.returncode == 0, out.stderr
     assert out.stdout.strip().endswith("CLEAN"), out.stdout
+
+
+def test_logit_bias_normalised():
+    # the device lists are bucketed by id: pairs in any order (or a dict)
+    # become ascending distinct ids; a repeated id is an error
+    from paged_moe_b200.params import ProcessorSettings
+    a = ProcessorSettings(logit_bias=((3, 4.0), (29999, 2.5), (1000, -3.0)))
+    b = ProcessorSettings.make(logit_bias={1000: -3.0, 3: 4.0, 29999: 2.5})
+    assert a.logit_bias == ((3, 4.0), (1000, -3.0), (29999, 2.5)) == b.logit_bias
+    assert a == b and hash(a) == hash(b)
+    with pytest.raises(ValueError):
+        ProcessorSettings(logit_bias=((5, 1.0), (5, 2.0)))
