@@ -2141,15 +2141,18 @@ int shard_stream_and_pack(const pm::SampleArgs& a, const pm::ShardK& sk, bool ca
 
 template <int KC>
 int launch_shard_merge(const pm::SampleArgs& a, const pm::MergeK& m, cudaStream_t st) {
-  constexpr int kWarpsM = 8;
-  const size_t smem = (sizeof(uint64_t) * pm::StreamMem<KC>::CAP + 1024) * kWarpsM;
+  // one CTA per row: the gathered keys of every shard, the row's top K, the
+  // radix histogram and its scalars
+  const size_t smem = sizeof(uint64_t) * ((size_t)m.n_shards * m.cand_k + KC) + sizeof(unsigned) * 256 +
+                      sizeof(int) * 8;
+  if (smem > 227 * 1024) return PM_ERR_UNSUPPORTED;
   static DeviceOnce once;
   once([&] {
-    cudaFuncSetAttribute(pm::k_shard_merge<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(pm::k_shard_merge<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
-  int64_t grid = (a.rows + kWarpsM - 1) / kWarpsM;
+  int64_t grid = a.rows;
   if (grid > (int64_t)num_sms() * 8) grid = (int64_t)num_sms() * 8;
-  pm::k_shard_merge<KC><<<(unsigned)grid, 32 * kWarpsM, smem, st>>>(a, m);
+  pm::k_shard_merge<KC><<<(unsigned)grid, 256, smem, st>>>(a, m);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? PM_OK : cuda_fail(e);
 }

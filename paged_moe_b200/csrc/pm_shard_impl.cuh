@@ -220,113 +220,125 @@ __device__ __forceinline__ void merge_lane_tiles(const MergeK& m, int64_t row, i
   }
 }
 
-// The merge: one warp per row over the gathered records of every shard.
+// The merge: one CTA per row over the gathered records of every shard.
+// Filtered rows: every shard's keys copied into shared memory by the whole
+// CTA and one block radix select of the row's top K (sorted); warp 0 then
+// computes the log-sum-exp and filters and draws as for the other modes.
 template <int KC>
 __global__ void __launch_bounds__(256) k_shard_merge(const __grid_constant__ SampleArgs a,
                                                      const __grid_constant__ MergeK m) {
-  constexpr int CAP = StreamMem<KC>::CAP;
-  struct MMem {
-    uint64_t cand[CAP];
-    unsigned hist[256];
-  };
   extern __shared__ __align__(128) unsigned char smem_smerge[];
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  MMem* mm = reinterpret_cast<MMem*>(smem_smerge) + wid;
-  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + wid; row < a.rows;
-       row += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+  uint64_t* U = reinterpret_cast<uint64_t*>(smem_smerge);   // [n_shards * cand_k] gathered keys
+  uint64_t* carry = U + (int64_t)m.n_shards * m.cand_k;     // [KC] the row's top K, sorted
+  unsigned* mhist = reinterpret_cast<unsigned*>(carry + KC);  // [256]
+  int* scal = reinterpret_cast<int*>(mhist + 256);          // [8]
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
     const pm_row_params p = row_params(a, row);
     const int mode = row_mode(p);
+    int ncarry = 0;
+    bool trimmed = false;
+    // warp 0: the row's log-sum-exp from the shards' tile statistics, while
+    // warps 1..7 gather the shards' keys
     float c = __int_as_float(0x7fc00000);
-    if (needs_xstats(a, p, mode)) {
-      LaneTiles lt;
-      merge_lane_tiles(m, row, m.xst, lt);
-      c = combine_lane_tiles(lt, lane_tiles_max(lt));
-    }
-    int tok = 0, ns = 0;
-    float x_tok = -INFINITY;
-    if (mode == kGreedy) {
-      uint64_t b = 0;
-      for (int s = lane; s < m.n_shards; s += 32) {
-        const uint64_t k = ld_cg(reinterpret_cast<const uint64_t*>(m.recs + s * m.shard_bytes + row * m.row_bytes));
-        b = k > b ? k : b;
+    if (wid == 0) {
+      if (needs_xstats(a, p, mode)) {
+        LaneTiles lt;
+        merge_lane_tiles(m, row, m.xst, lt);
+        c = combine_lane_tiles(lt, lane_tiles_max(lt));
       }
-      b = warp_max_u64(b);
-      tok = (int)key_index(b);
-      x_tok = key_value(b);
-    } else if (mode == kCand) {
+    }
+    if (mode == kCand) {
       const int K = (p.top_k > 0 && p.top_k < KC) ? p.top_k : KC;
-      Cand cd;
-      cand_reset(cd);
-      bool trimmed = false;
+      int off = 0;
       for (int s = 0; s < m.n_shards; ++s) {
         const unsigned char* rec = m.recs + s * m.shard_bytes + row * m.row_bytes;
         const uint32_t hdr = ld_cg(reinterpret_cast<const uint32_t*>(rec + 8));
         trimmed |= (hdr >> 31) != 0;
         const int n = (int)(hdr & 0x7fffffffu);
         const uint64_t* keys = reinterpret_cast<const uint64_t*>(rec + m.keys);
-        for (int i0 = 0; i0 < n; i0 += 32)
-          cand_offer_key<CAP>(i0 + lane < n ? ld_cg(&keys[i0 + lane]) : 0ull, mm->cand, mm->hist, cd, K);
+        if (wid > 0)
+          for (int i = tid - 32; i < n; i += blockDim.x - 32) U[off + i] = ld_cg(&keys[i]);
+        off += n;
       }
-      if (cd.cnt > K) cand_compact<CAP>(mm->cand, mm->hist, cd, K);
-      warp_sort_desc(mm->cand, cd.cnt);
-      tok = warp_filter_draw(a, p, row, mm->cand, cd.cnt, !(trimmed || cd.trimmed), c, &ns);
-      if (tok >= 0) {
-        float fx = -INFINITY;
-        for (int r = lane; r < cd.cnt; r += 32)
-          if ((int)key_index(mm->cand[r]) == tok) fx = key_value(mm->cand[r]);
-        x_tok = warp_max(fx);
-        if (a.surv_ids && lane == 0) write_survivors(a, p, row, mm->cand, ns);
-      }
-    } else {
-      // tile by the first uniform over the global tile weights, token from
-      // the tile's own draw
-      LaneTiles lt;
-      merge_lane_tiles(m, row, m.yst, lt);
-      const float my = lane_tiles_max(lt);
-      if (my > -INFINITY) {
-        int sh = 1;
-        while ((1 << (sh - 1)) < m.nt) ++sh;
-        const double scale = __longlong_as_double((long long)(1023 - sh) << 52);  // 2^-sh
-        uint64_t w[kMaxPer];
-        uint64_t lsum = 0;
-#pragma unroll
-        for (int i = 0; i < kMaxPer; ++i) {
-          w[i] = i < lt.per ? __double2ull_rz(dmul(tile_weight_of(lt.m[i], lt.s[i], my), scale)) : 0ull;
-          lsum += w[i];
+      __syncthreads();
+      ncarry = block_topk_sorted(U, off, K, carry, KC, mhist, scal);
+      trimmed = trimmed || off > K;
+      __syncthreads();
+    }
+    if (wid == 0) {
+      int tok = 0, ns = 0;
+      float x_tok = -INFINITY;
+      if (mode == kGreedy) {
+        uint64_t b = 0;
+        for (int s = lane; s < m.n_shards; s += 32) {
+          const uint64_t k = ld_cg(reinterpret_cast<const uint64_t*>(m.recs + s * m.shard_bytes + row * m.row_bytes));
+          b = k > b ? k : b;
         }
-        const uint64_t incl = warp_incl_scan_u64(lsum);
-        const uint64_t W = __shfl_sync(kFull, incl, 31);
-        const uint64_t t1 = scale_u53(row_u53(a, row, 0), W);
-        const unsigned hit = __ballot_sync(kFull, incl > t1);
-        const int src = hit ? __ffs(hit) - 1 : 31;
-        int tt = m.nt - 1;
-        if (lane == src) {
-          uint64_t run = incl - lsum;
-          int found = -1;
-#pragma unroll
+        b = warp_max_u64(b);
+        tok = (int)key_index(b);
+        x_tok = key_value(b);
+      } else if (mode == kCand) {
+        tok = warp_filter_draw(a, p, row, carry, ncarry, !trimmed, c, &ns);
+        if (tok >= 0) {
+          float fx = -INFINITY;
+          for (int r = lane; r < ncarry; r += 32)
+            if ((int)key_index(carry[r]) == tok) fx = key_value(carry[r]);
+          x_tok = warp_max(fx);
+          if (a.surv_ids && lane == 0) write_survivors(a, p, row, carry, ns);
+        }
+      } else {
+        // tile by the first uniform over the global tile weights, token from
+        // the tile's own draw
+        LaneTiles lt;
+        merge_lane_tiles(m, row, m.yst, lt);
+        const float my = lane_tiles_max(lt);
+        if (my > -INFINITY) {
+          int sh = 1;
+          while ((1 << (sh - 1)) < m.nt) ++sh;
+          const double scale = __longlong_as_double((long long)(1023 - sh) << 52);  // 2^-sh
+          uint64_t w[kMaxPer];
+          uint64_t lsum = 0;
+  #pragma unroll
           for (int i = 0; i < kMaxPer; ++i) {
-            run += w[i];
-            if (found < 0 && i < lt.per && run > t1) found = i;
+            w[i] = i < lt.per ? __double2ull_rz(dmul(tile_weight_of(lt.m[i], lt.s[i], my), scale)) : 0ull;
+            lsum += w[i];
           }
-          tt = lane * lt.per + (found < 0 ? 0 : found);
+          const uint64_t incl = warp_incl_scan_u64(lsum);
+          const uint64_t W = __shfl_sync(kFull, incl, 31);
+          const uint64_t t1 = scale_u53(row_u53(a, row, 0), W);
+          const unsigned hit = __ballot_sync(kFull, incl > t1);
+          const int src = hit ? __ffs(hit) - 1 : 31;
+          int tt = m.nt - 1;
+          if (lane == src) {
+            uint64_t run = incl - lsum;
+            int found = -1;
+  #pragma unroll
+            for (int i = 0; i < kMaxPer; ++i) {
+              run += w[i];
+              if (found < 0 && i < lt.per && run > t1) found = i;
+            }
+            tt = lane * lt.per + (found < 0 ? 0 : found);
+          }
+          tt = __shfl_sync(kFull, tt, src);
+          if (tt >= m.nt) tt = m.nt - 1;
+          const int s = min(tt / m.nts, m.n_shards - 1);
+          const int tl = tt - s * m.nts;
+          const unsigned char* rec = m.recs + s * m.shard_bytes + row * m.row_bytes;
+          tok = ld_cg(reinterpret_cast<const int32_t*>(rec + m.ttok) + tl);
+          x_tok = ld_cg(reinterpret_cast<const float*>(rec + m.tx) + tl);
         }
-        tt = __shfl_sync(kFull, tt, src);
-        if (tt >= m.nt) tt = m.nt - 1;
-        const int s = min(tt / m.nts, m.n_shards - 1);
-        const int tl = tt - s * m.nts;
-        const unsigned char* rec = m.recs + s * m.shard_bytes + row * m.row_bytes;
-        tok = ld_cg(reinterpret_cast<const int32_t*>(rec + m.ttok) + tl);
-        x_tok = ld_cg(reinterpret_cast<const float*>(rec + m.tx) + tl);
       }
+      if (lane == 0) {
+        a.status[row] = tok < 0 ? 1 : 0;
+        a.tokens[row] = tok;
+        if (a.lse_out) a.lse_out[row] = c;
+        if (a.tok_logprob) a.tok_logprob[row] = tok >= 0 ? fsub(x_tok, c) : __int_as_float(0x7fc00000);
+        if (a.n_surv && (mode != kCand || !a.surv_ids)) a.n_surv[row] = mode == kCand ? ns : 0;
+      }
+      __syncwarp();
     }
-    if (lane == 0) {
-      a.status[row] = tok < 0 ? 1 : 0;
-      a.tokens[row] = tok;
-      if (a.lse_out) a.lse_out[row] = c;
-      if (a.tok_logprob) a.tok_logprob[row] = tok >= 0 ? fsub(x_tok, c) : __int_as_float(0x7fc00000);
-      if (a.n_surv && (mode != kCand || !a.surv_ids)) a.n_surv[row] = mode == kCand ? ns : 0;
-    }
-    __syncwarp();
+    __syncthreads();
   }
 }
 
