@@ -2041,8 +2041,8 @@ int pm_verify(const pm_rows* rows, const pm_noise* noise, const pm_verify_args* 
     else pm::k_residual_tiles<float, float><<<(unsigned)g1, 256, 0, st>>>(a, da, vk);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
-    int64_t g2 = (V.B + 7) / 8;
-    if (g2 > (int64_t)num_sms() * 8) g2 = (int64_t)num_sms() * 8;
+    int64_t g2 = V.B;  // one CTA per request
+    if (g2 > (int64_t)num_sms() * 4) g2 = (int64_t)num_sms() * 4;
     if (tb) pm::k_residual_draw<__nv_bfloat16><<<(unsigned)g2, 256, 0, st>>>(a, vk);
     else pm::k_residual_draw<float><<<(unsigned)g2, 256, 0, st>>>(a, vk);
     e = cudaGetLastError();

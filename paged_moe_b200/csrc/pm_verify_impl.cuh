@@ -253,9 +253,10 @@ __global__ void __launch_bounds__(256) k_verify_accept(const __grid_constant__ S
 // Whole-vocabulary residual draw, tile-parallel.  k_residual_tiles: one
 // warp per (request, tile) of every request with a pending row: the tile's
 // sum of floor(max(fl32(p - q), 0) 2^52), p = expf(fl32(y - c_y)),
-// q = expf(fl32(d - c_d)).  k_residual_draw: one warp per pending request:
+// q = expf(fl32(d - c_d)).  k_residual_draw: one CTA per pending request:
 // the tile whose inclusive prefix first exceeds floor(u R), then the token
-// inside it the same way (no positive residual: the row's own draw).
+// inside it the same way, the tile's 1,024 masses computed by all eight
+// warps (no positive residual: the row's own draw).
 template <typename T, typename TD>
 __global__ void __launch_bounds__(256) k_residual_tiles(const __grid_constant__ SampleArgs a,
                                                         const __grid_constant__ SampleArgs da,
@@ -307,87 +308,104 @@ template <typename T>
 __global__ void __launch_bounds__(256) k_residual_draw(const __grid_constant__ SampleArgs a,
                                                        const __grid_constant__ VerifyK v) {
   constexpr int VW = Lay<T>::VW;
-  const int lane = threadIdx.x & 31;
+  __shared__ uint64_t qbuf[kTile];  // the chosen tile's residual masses in token order
+  __shared__ uint64_t wtot[8];
+  __shared__ uint64_t s_t2;
+  __shared__ int s_tt, s_tok;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int K1 = v.k + 1;
   const int64_t B = a.rows / K1;
   const int nt = a.n_tiles;
-  for (int64_t b = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < B;
-       b += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
     const int j = ld_cg(&v.pending[b]);
-    if (j < 0) continue;
+    if (j < 0) continue;  // uniform over the CTA
     const int64_t row = b * K1 + j;
     const int64_t drow = b * v.k + j;
     const pm_row_params p = row_params(a, row);
     const float cy = ld_cg(&v.ylse[b]);
     const float cd = ld_cg(&v.dlse[drow]);
-    const uint64_t* rs = v.rsum + b * nt;
-    uint64_t R = 0;
-    for (int t = lane; t < nt; t += 32) R += ld_cg(&rs[t]);
-    R = warp_sum_u64(R);
-    int tok = ld_cg(&v.rtok[row]);
-    if (R > 0) {
-      const uint64_t tgt = scale_u53(residual_u53(a, v, b, row), R);
+    // warp 0: the tile whose inclusive prefix of the tile sums first exceeds
+    // floor(u R), and the target left inside it
+    if (wid == 0) {
+      const uint64_t* rs = v.rsum + b * nt;
+      uint64_t R = 0;
+      for (int t = lane; t < nt; t += 32) R += ld_cg(&rs[t]);
+      R = warp_sum_u64(R);
       int tt = -1;
       uint64_t t2 = 0;
-      uint64_t carry = 0;
-      for (int t0 = 0; t0 < nt; t0 += 32) {
-        const int t = t0 + lane;
-        const uint64_t wv = t < nt ? ld_cg(&rs[t]) : 0ull;
-        const uint64_t incl = carry + warp_incl_scan_u64(wv);
-        const unsigned hit = __ballot_sync(kFull, t < nt && incl > tgt);
-        if (hit) {
-          const int src = __ffs(hit) - 1;
-          tt = t0 + src;
-          t2 = tgt - (__shfl_sync(kFull, incl, src) - __shfl_sync(kFull, wv, src));
-          break;
-        }
-        carry = __shfl_sync(kFull, incl, 31);
-      }
-      if (tt >= 0) {
-        TileIn ti;
-        load_tile<T>(a, row, tt, ti);
-        process_tile_regs<VW>(a, p, row, tt, ti);
-        const int64_t start = (int64_t)tt * kTile;
-        const int n_valid = tile_valid(a, tt);
-        uint64_t acc = 0;
-        for (int jj = 0; jj < 32 / VW; ++jj) {
-          uint64_t q[VW];
-          uint64_t ls = 0;
-#pragma unroll
-          for (int c = 0; c < VW; ++c) {
-            const int e = jj * 32 * VW + lane * VW + c;
-            q[c] = 0;
-            if (e < n_valid) {
-              const float x = ti.v[jj * VW + c];
-              const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
-              q[c] = residual_q52(det_expf(fsub(y, cy)), draft_prob(v, drow, start + e, cd));
-            }
-            ls += q[c];
-          }
-          const uint64_t incl = acc + warp_incl_scan_u64(ls);
-          const unsigned hit = __ballot_sync(kFull, incl > t2);
+      if (R > 0) {
+        const uint64_t tgt = scale_u53(residual_u53(a, v, b, row), R);
+        uint64_t carry = 0;
+        for (int t0 = 0; t0 < nt; t0 += 32) {
+          const int t = t0 + lane;
+          const uint64_t wv = t < nt ? ld_cg(&rs[t]) : 0ull;
+          const uint64_t incl = carry + warp_incl_scan_u64(wv);
+          const unsigned hit = __ballot_sync(kFull, t < nt && incl > tgt);
           if (hit) {
             const int src = __ffs(hit) - 1;
-            int found = 0;
-            if (lane == src) {
-              uint64_t run = incl - ls;
-              found = -1;
-#pragma unroll
-              for (int c = 0; c < VW; ++c) {
-                run += q[c];
-                if (found < 0 && run > t2) found = c;
-              }
-            }
-            found = __shfl_sync(kFull, found, src);
-            tok = (int)(start + jj * 32 * VW + src * VW + found);
+            tt = t0 + src;
+            t2 = tgt - (__shfl_sync(kFull, incl, src) - __shfl_sync(kFull, wv, src));
             break;
           }
-          acc = __shfl_sync(kFull, incl, 31);
+          carry = __shfl_sync(kFull, incl, 31);
+        }
+      }
+      if (lane == 0) {
+        s_tt = tt;
+        s_t2 = t2;
+        s_tok = ld_cg(&v.rtok[row]);  // no positive residual: the row's own draw
+      }
+    }
+    __syncthreads();
+    const int tt = s_tt;
+    if (tt >= 0) {
+      // every warp loads and processes the tile; warp w computes the masses of
+      // its four slots a lane (128 tokens), stored by token index
+      TileIn ti;
+      load_tile<T>(a, row, tt, ti);
+      process_tile_regs<VW>(a, p, row, tt, ti);
+      const int64_t start = (int64_t)tt * kTile;
+      const int n_valid = tile_valid(a, tt);
+#pragma unroll
+      for (int k4 = 0; k4 < 4; ++k4) {
+        const int sl = wid * 4 + k4;
+        const int e = slot_elem<VW>(sl, lane);
+        uint64_t q = 0;
+        if (e < n_valid) {
+          const float x = ti.v[sl];
+          const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
+          q = residual_q52(det_expf(fsub(y, cy)), draft_prob(v, drow, start + e, cd));
+        }
+        qbuf[e] = q;
+      }
+      __syncthreads();
+      // the token whose inclusive prefix first exceeds t2: thread t scans
+      // tokens [4 t, 4 t + 4) after a block scan of the four-token sums
+      uint64_t loc = 0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) loc += qbuf[4 * tid + c];
+      const uint64_t wincl = warp_incl_scan_u64(loc);
+      if (lane == 31) wtot[wid] = wincl;
+      __syncthreads();
+      uint64_t base = 0;
+      for (int w = 0; w < wid; ++w) base += wtot[w];
+      const uint64_t excl = base + wincl - loc;
+      const uint64_t t2 = s_t2;
+      if (excl <= t2 && t2 < excl + loc) {
+        uint64_t run = excl;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          run += qbuf[4 * tid + c];
+          if (run > t2) {
+            s_tok = (int)(start + 4 * tid + c);
+            break;
+          }
         }
       }
     }
-    if (lane == 0) v.tokens[b * K1 + j] = tok;
-    __syncwarp();
+    __syncthreads();
+    if (tid == 0) v.tokens[b * K1 + j] = s_tok;
+    __syncthreads();
   }
 }
 
