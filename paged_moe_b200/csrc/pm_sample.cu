@@ -795,6 +795,77 @@ __global__ void __launch_bounds__(256) k_row_merge_cta(const __grid_constant__ S
                                                   owner_warp(row * a.n_tiles, total, a.n_warps) + 1);
     const pm_row_params p = row_params(a, row);
     const int mode = row_mode(p);
+    if (mode == kFullDraw) {
+      // whole-vocabulary draw: warp 0 the log-sum-exp (when asked), warp 1
+      // the tile; then all eight warps the tile's q52 masses (four slots a
+      // lane each, stored by token index) and a block scan for the token
+      constexpr int VW = Lay<T>::VW;
+      uint64_t* qbuf = &mc->cand[0][0];                            // [1024] masses
+      float* xbuf = reinterpret_cast<float*>(&mc->cand[0][0] + kTile);  // [1024] processed logits
+      const bool needx = needs_xstats(a, p, mode);
+      if (wid == 0 && needx) {
+        float mx;
+        const float c = warp_combine(a.statx + row * a.n_tiles, a.n_tiles, &mx);
+        if (lane == 0) mc->lse = c;
+      } else if (wid == 1) {
+        float mt;
+        uint64_t t2;
+        const int tt = warp_full_pick(a, row, &mt, &t2);
+        if (lane == 0) {
+          mc->scal[0] = tt;
+          mc->scal[1] = tt >= 0 ? tt * kTile : 0;
+          mc->scal[2] = __float_as_int(mt);
+          mc->scal[3] = __float_as_int(-INFINITY);
+          mc->u[0] = t2;
+        }
+      }
+      __syncthreads();
+      const int tt = mc->scal[0];
+      if (tt >= 0) {
+        const float mt = __int_as_float(mc->scal[2]);
+        TileIn ti;
+        load_tile<T>(a, row, tt, ti);
+        process_tile_regs<VW>(a, p, row, tt, ti);
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int sl = wid * 4 + k4;
+          const int e = slot_elem<VW>(sl, lane);
+          const float x = ti.v[sl];
+          const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
+          qbuf[e] = q52(fsub(y, mt));
+          xbuf[e] = x;
+        }
+        __syncthreads();
+        uint64_t loc = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) loc += qbuf[4 * tid + c];
+        const uint64_t wincl = warp_incl_scan_u64(loc);
+        if (lane == 31) mc->u[1 + wid] = wincl;
+        __syncthreads();
+        uint64_t base = 0;
+        for (int w = 0; w < wid; ++w) base += mc->u[1 + w];
+        const uint64_t excl = base + wincl - loc;
+        const uint64_t t2 = mc->u[0];
+        if (excl <= t2 && t2 < excl + loc) {
+          uint64_t run = excl;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            run += qbuf[4 * tid + c];
+            if (run > t2) {
+              mc->scal[1] = tt * kTile + 4 * tid + c;
+              mc->scal[3] = __float_as_int(xbuf[4 * tid + c]);
+              break;
+            }
+          }
+        }
+      }
+      __syncthreads();
+      if (tid == 0)
+        write_row(a, row, mode, mc->scal[1], __int_as_float(mc->scal[3]), needx ? mc->lse : __int_as_float(0x7fc00000),
+                  0);
+      __syncthreads();
+      continue;
+    }
     if (mode != kCand) {
       if (wid == 0) {
         float x_tok, lse;

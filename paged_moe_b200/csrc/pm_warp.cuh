@@ -551,17 +551,19 @@ __device__ __forceinline__ void process_tile_regs(const SampleArgs& a, const pm_
   }
 }
 
-template <typename T>
-__device__ __noinline__ int warp_full_draw(const SampleArgs& a, const pm_row_params& p, int64_t row, float* x_out) {
-  constexpr int VW = Lay<T>::VW;
+// The tile of a whole-vocabulary draw: the first whose inclusive prefix of
+// integer tile weights (over the row's y statistics) exceeds the row's first
+// 53-bit uniform scaled to their sum, by one warp.  Returns the tile (-1: no
+// finite value in the row) and, in every lane, the tile's maximum and the
+// target of the token search inside it.
+__device__ __forceinline__ int warp_full_pick(const SampleArgs& a, int64_t row, float* mt_out, uint64_t* t2_out) {
   const int lane = threadIdx.x & 31;
   const int nt = a.n_tiles;
   const TileStat* st = a.staty + row * (int64_t)nt;
   LaneTiles lt;
   load_lane_tiles(st, nt, lt);
   const float my = lane_tiles_max(lt);
-  *x_out = -INFINITY;
-  if (!(my > -INFINITY)) return 0;
+  if (!(my > -INFINITY)) return -1;
   int sh = 1;
   while ((1 << (sh - 1)) < nt) ++sh;
   const double scale = __longlong_as_double((long long)(1023 - sh) << 52);  // 2^-sh
@@ -592,8 +594,20 @@ __device__ __noinline__ int warp_full_draw(const SampleArgs& a, const pm_row_par
   }
   tt = __shfl_sync(kFull, tt, src);
   if (tt >= nt) tt = nt - 1;
-  const float mt = ld_cg(&st[tt].m);
-  const uint64_t t2 = scale_u53(row_u53(a, row, 1), ld_cg(&st[tt].s));
+  *mt_out = ld_cg(&st[tt].m);
+  *t2_out = scale_u53(row_u53(a, row, 1), ld_cg(&st[tt].s));
+  return tt;
+}
+
+template <typename T>
+__device__ __noinline__ int warp_full_draw(const SampleArgs& a, const pm_row_params& p, int64_t row, float* x_out) {
+  constexpr int VW = Lay<T>::VW;
+  const int lane = threadIdx.x & 31;
+  *x_out = -INFINITY;
+  float mt;
+  uint64_t t2;
+  const int tt = warp_full_pick(a, row, &mt, &t2);
+  if (tt < 0) return 0;
   const int64_t start = (int64_t)tt * kTile;
   TileIn ti;
   load_tile<T>(a, row, tt, ti);
