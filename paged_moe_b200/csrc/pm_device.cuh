@@ -138,6 +138,29 @@ __device__ __forceinline__ void q52x2(float d0, float d1, uint64_t& q0, uint64_t
   q1 = q52_from_bits((uint32_t)(P >> 32) + (k1 << 23));
 }
 
+// det_expf of two values at once (packed f32x2: each half is the same IEEE
+// fp32 sequence as det_expf); bit-identical to two det_expf calls.
+__device__ __forceinline__ void det_expf_x2(float d0, float d1, float& e0, float& e1) {
+  const bool z0 = !(d0 >= -87.0f), z1 = !(d1 >= -87.0f);
+  const uint64_t D = pk(z0 ? 0.0f : d0, z1 ? 0.0f : d1);
+  const uint64_t T = mul2(D, pk(0x1.715476p+0f, 0x1.715476p+0f));
+  const uint64_t TM = add2(T, pk(12582912.0f, 12582912.0f));
+  const uint64_t KF = add2(TM, pk(-12582912.0f, -12582912.0f));
+  uint64_t R = fma2(KF, pk(-0x1.62e4p-1f, -0x1.62e4p-1f), D);
+  R = fma2(KF, pk(-0x1.7f7d1cp-20f, -0x1.7f7d1cp-20f), R);
+  uint64_t P = pk(0x1.a01a02p-13f, 0x1.a01a02p-13f);
+  P = fma2(P, R, pk(0x1.6c16c2p-10f, 0x1.6c16c2p-10f));
+  P = fma2(P, R, pk(0x1.111112p-7f, 0x1.111112p-7f));
+  P = fma2(P, R, pk(0x1.555556p-5f, 0x1.555556p-5f));
+  P = fma2(P, R, pk(0x1.555556p-3f, 0x1.555556p-3f));
+  P = fma2(P, R, pk(0x1.0p-1f, 0x1.0p-1f));
+  P = fma2(P, R, pk(1.0f, 1.0f));
+  P = fma2(P, R, pk(1.0f, 1.0f));
+  const uint32_t k0 = (uint32_t)TM - 0x4B400000u, k1 = (uint32_t)(TM >> 32) - 0x4B400000u;
+  e0 = z0 ? 0.0f : __uint_as_float((uint32_t)P + (k0 << 23));
+  e1 = z1 ? 0.0f : __uint_as_float((uint32_t)(P >> 32) + (k1 << 23));
+}
+
 // e^d in fp64 for d <= ~0; d < -700 or NaN -> 0.
 __device__ __forceinline__ double det_exp64(double d) {
   if (!(d >= -700.0)) return 0.0;

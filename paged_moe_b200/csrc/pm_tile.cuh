@@ -228,7 +228,11 @@ __device__ __forceinline__ void tile_stats(const float (&v)[32], float* m_out, u
   uint64_t sum = 0;
   if (m > -INFINITY) {
 #pragma unroll
-    for (int s = 0; s < 32; ++s) sum += q52(fsub(v[s], m));
+    for (int s = 0; s < 32; s += 2) {
+      uint64_t q0, q1;
+      q52x2(fsub(v[s], m), fsub(v[s + 1], m), q0, q1);
+      sum += q0 + q1;
+    }
   }
   *m_out = m;
   *s_out = warp_sum_u64(sum);

@@ -288,16 +288,21 @@ __global__ void __launch_bounds__(256) k_residual_tiles(const __grid_constant__ 
     const int n_valid = tile_valid(a, t);
     uint64_t s = 0;
 #pragma unroll
-    for (int sl = 0; sl < 32; ++sl) {
-      const int e = slot_elem<VW>(sl, lane);
-      if (e < n_valid) {
-        const float x = ti.v[sl];
-        const float y = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
-        float dv;
-        if constexpr (same) dv = td.v[sl];
-        else dv = draft_value(v, drow, start + e);
-        s += residual_q52(det_expf(fsub(y, cy)), det_expf(fsub(dv, cd)));
+    for (int sl = 0; sl < 32; sl += 2) {
+      float y2[2], d2[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int e = slot_elem<VW>(sl + h, lane);
+        const float x = ti.v[sl + h];
+        y2[h] = x > -INFINITY ? fmul(x, p.inv_temperature) : -INFINITY;
+        if constexpr (same) d2[h] = td.v[sl + h];
+        else d2[h] = e < n_valid ? draft_value(v, drow, start + e) : -INFINITY;
       }
+      float p0, p1, q0, q1;
+      det_expf_x2(fsub(y2[0], cy), fsub(y2[1], cy), p0, p1);
+      det_expf_x2(fsub(d2[0], cd), fsub(d2[1], cd), q0, q1);
+      if (slot_elem<VW>(sl, lane) < n_valid) s += residual_q52(p0, q0);
+      if (slot_elem<VW>(sl + 1, lane) < n_valid) s += residual_q52(p1, q1);
     }
     s = warp_sum_u64(s);
     if (lane == 0) v.rsum[w] = s;
