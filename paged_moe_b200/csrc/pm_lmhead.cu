@@ -680,8 +680,12 @@ __global__ void __cluster_dims__(kLCluster, 1, 1) __launch_bounds__(kLThreads, 2
       uint64_t* dst = a.cand + (row * a.max_parts + part) * (int64_t)KC;
       int cnt = 0, ties = 0;
       uint64_t theta = 0;
+      // a half whose maximum lies below the threshold's value emits nothing:
+      // when no lane of the warp can emit, the sweep is skipped
+      const bool idle = path == 0 || !(mh >= tv);
+      const int nsweep = __all_sync(kFull, idle) ? 0 : nch;
 #pragma unroll 1
-      for (int c = 0; c < nch; ++c) {
+      for (int c = 0; c < nsweep; ++c) {
         float v[32];
         chunk(c, v);
         if (path != 0) {
