@@ -741,6 +741,35 @@ __device__ __forceinline__ void part_end(const SampleArgs& a, int64_t row, int64
     const uint64_t k = rankkey(ps.best_x, (uint32_t)ps.best_e);
     const uint64_t wk = warp_max_u64(k);
     if (lane == 0) a.best[row * a.max_parts + part] = wk;
+    if (a.merge_greedy) {
+      // the last part of the row to finish merges it (its own key and
+      // statistics are ordered before the count by the fence; the others'
+      // before theirs)
+      const int n_parts = (int)(owner_warp((row + 1) * a.n_tiles - 1, total, a.n_warps) -
+                                owner_warp(row * a.n_tiles, total, a.n_warps) + 1);
+      int last = 0;
+      if (lane == 0) {
+        __threadfence();
+        const unsigned long long done = atomicAdd(reinterpret_cast<unsigned long long*>(&a.row_tau[row]), 1ull);
+        last = done == (unsigned long long)(n_parts - 1);
+        __threadfence();
+      }
+      last = __shfl_sync(kFull, last, 0);
+      if (last) {
+        uint64_t bk = 0;
+        for (int i = lane; i < n_parts; i += 32) {
+          const uint64_t kk = ld_cg(&a.best[row * a.max_parts + i]);
+          bk = kk > bk ? kk : bk;
+        }
+        bk = warp_max_u64(bk);
+        float c = __int_as_float(0x7fc00000);
+        if (needs_xstats(a, ps.p, kGreedy)) {
+          float mx;
+          c = warp_combine(a.statx + row * a.n_tiles, a.n_tiles, &mx);
+        }
+        if (lane == 0) write_row(a, row, kGreedy, (int)key_index(bk), key_value(bk), c, 0);
+      }
+    }
   } else if (ps.mode == kCand) {
     if (ps.needa) approx_part_end(a, row, ps);
     if (ps.cd.cnt > ps.K) cand_compact<CAP>(wm->cand, wm->hist, ps.cd, ps.K);
@@ -1623,11 +1652,12 @@ int launch_stream(pm::SampleArgs a, bool cand_rows, cudaStream_t st, bool merge 
     const size_t sb = sizeof(int32_t) * a.rows, tb = sizeof(uint64_t) * a.rows,
                  xb = sizeof(int32_t) * (1 + a.rows);
     const bool adjacent = t0 >= s0 + sb && t0 <= s0 + sb + 256 && x0 >= t0 + tb && x0 <= t0 + tb + 256;
-    if ((cand_rows || a.approx_ok) && adjacent) {
+    // (row_tau also counts the finished parts of greedy rows merged in the pass)
+    if ((cand_rows || a.approx_ok || a.merge_greedy) && adjacent) {
       e = cudaMemsetAsync(a.status, 0, (size_t)(x0 - s0) + (a.approx_ok ? xb : 0), st);
     } else {
       e = cudaMemsetAsync(a.status, 0, sb, st);
-      if (e == cudaSuccess && cand_rows) e = cudaMemsetAsync(a.row_tau, 0, tb, st);
+      if (e == cudaSuccess && (cand_rows || a.merge_greedy)) e = cudaMemsetAsync(a.row_tau, 0, tb, st);
       if (e == cudaSuccess && a.approx_ok) e = cudaMemsetAsync(a.exact_q, 0, xb, st);
     }
     if (e != cudaSuccess) return cuda_fail(e);
@@ -1659,10 +1689,12 @@ int launch_stream(pm::SampleArgs a, bool cand_rows, cudaStream_t st, bool merge 
   return launch_merges<T, KC>(a, st);
 }
 
-int launch_stream_any(int dtype, int KC, const pm::SampleArgs& a, bool cand_rows, cudaStream_t st) {
+int launch_stream_any(int dtype, int KC, const pm::SampleArgs& a, bool cand_rows, cudaStream_t st,
+                      bool merge = true) {
   const bool bf = dtype == PM_DTYPE_BF16;
-  if (KC == 64) return bf ? launch_stream<__nv_bfloat16, 64>(a, cand_rows, st) : launch_stream<float, 64>(a, cand_rows, st);
-  return bf ? launch_stream<__nv_bfloat16, 256>(a, cand_rows, st) : launch_stream<float, 256>(a, cand_rows, st);
+  if (KC == 64)
+    return bf ? launch_stream<__nv_bfloat16, 64>(a, cand_rows, st, merge) : launch_stream<float, 64>(a, cand_rows, st, merge);
+  return bf ? launch_stream<__nv_bfloat16, 256>(a, cand_rows, st, merge) : launch_stream<float, 256>(a, cand_rows, st, merge);
 }
 
 // Masked rows go through the one-CTA-per-row gather pass when their logits
@@ -1691,13 +1723,19 @@ int launch_wide(const pm::SampleArgs& a, cudaStream_t st) {
 // The sampling pass over prepared arguments: gather pass for masked rows,
 // streaming + merge otherwise; then, when some row has an unbounded filter,
 // the exact finish of rows whose survivors outran the candidates.
-int launch_rows(const pm_rows* r, int KC, const pm::SampleArgs& a, cudaStream_t st) {
+int launch_rows(const pm_rows* r, int KC, const pm::SampleArgs& a0, cudaStream_t st) {
   const bool bf = r->dtype == PM_DTYPE_BF16;
   int rc;
+  pm::SampleArgs a = a0;
   if (masked_path(r)) {
     rc = pm_launch_masked(r->dtype, KC, a, st);
   } else {
-    rc = launch_stream_any(r->dtype, KC, a, has_cand_rows(r), st);
+    // greedy rows are merged inside the streaming pass; when every row is
+    // greedy (no filter of any row, no whole-vocabulary draw) the merge
+    // kernel has nothing left to do and is not launched
+    a.merge_greedy = true;
+    const bool all_greedy = !(r->flags_any & (PM_F_TOP_P | PM_F_MIN_P | PM_F_FULL)) && r->top_k_max <= 0;
+    rc = launch_stream_any(r->dtype, KC, a, has_cand_rows(r), st, !all_greedy);
   }
   if (rc) return rc;
   if (r->flags_any & PM_F_UNBOUNDED) {

@@ -83,6 +83,10 @@ struct SampleArgs {
   // a rigorous bracket around the exact log-sum-exp, and the rare rows whose
   // cut the bracket does not decide are queued for the exact pass
   bool approx_ok;
+  // greedy rows finished inside the streaming pass: the warp that ends a
+  // row's last part (a count of finished parts in row_tau, which greedy rows
+  // do not otherwise use) takes the parts' best keys and writes the row
+  bool merge_greedy;
   int32_t* exact_q;  // [1 + 2 rows]: queued count, per-entry tile counters [rows], queued rows [rows]
   int32_t n_tiles;
   int32_t max_parts;
