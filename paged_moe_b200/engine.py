@@ -38,6 +38,26 @@ def workspace(nbytes: int, device: torch.device, stream: Optional[torch.cuda.Str
         return buf
 
 
+_size_cache: dict = {}
+
+
+def cached_size(key, query) -> int:
+    """A workspace size that depends only on shapes and settings (key),
+    queried from the library once per key."""
+    v = _size_cache.get(key)
+    if v is None:
+        v = int(query())
+        with _ws_lock:
+            if len(_size_cache) > 1024:
+                _size_cache.clear()
+            _size_cache[key] = v
+    return v
+
+
+def _shape(t: Optional[torch.Tensor]):
+    return None if t is None else tuple(t.shape)
+
+
 def _dtype_code(t: torch.Tensor) -> int:
     if t.dtype == torch.float32:
         return L.PM_DTYPE_F32
@@ -286,7 +306,10 @@ def sample_rows(logits: torch.Tensor, sampler: Union[SamplerSettings, Sequence[S
         g = keep(gumbel.to(device=dev, dtype=torch.float32).contiguous())
     if uniform is not None:
         u = keep(uniform.to(device=dev, dtype=torch.float64).contiguous())
-    nbytes = E.sample_workspace_bytes(q.logits, q.params, q.per_row, q.flags_any, q.top_k_max, q.hist, q.mask)
+    key = ("sample", dev.index, tuple(q.logits.shape), q.logits.stride(0), q.logits.dtype, q.per_row, q.flags_any,
+           q.top_k_max, _shape(q.hist), _shape(q.mask))
+    nbytes = cached_size(key, lambda: E.sample_workspace_bytes(q.logits, q.params, q.per_row, q.flags_any,
+                                                              q.top_k_max, q.hist, q.mask))
     if nbytes == 0:
         L.check(L.PM_ERR_UNSUPPORTED, "pm_sample_workspace_bytes")
     ws = workspace(nbytes, dev)

@@ -20,7 +20,7 @@ from typing import Optional
 import torch
 
 from . import _lib as L
-from .engine import _i64, _Keep, prepare, workspace
+from .engine import _i64, _Keep, cached_size, prepare, workspace
 
 _MODES = {"match": L.PM_VERIFY_MATCH, "residual": L.PM_VERIFY_RESIDUAL}
 
@@ -102,8 +102,12 @@ def verify(target_logits: torch.Tensor, drafts: torch.Tensor, y: torch.Tensor, s
         ur = keep(torch.as_tensor(u_residual).to(device=dev, dtype=torch.float64).reshape(B).contiguous())
     E = L.ext()
     m = _MODES[mode]
-    nbytes = E.verify_workspace_bytes(q.logits, q.params, q.per_row, q.flags_any, q.top_k_max, q.hist, q.feed,
-                                      q.feed_group, q.mask, m, drafts)
+    key = ("verify", dev.index, tuple(q.logits.shape), q.logits.stride(0), q.logits.dtype, q.per_row, q.flags_any,
+           q.top_k_max, None if q.hist is None else tuple(q.hist.shape), None if q.feed is None else tuple(q.feed.shape),
+           q.feed_group, None if q.mask is None else tuple(q.mask.shape), m, tuple(drafts.shape))
+    nbytes = cached_size(key, lambda: E.verify_workspace_bytes(q.logits, q.params, q.per_row, q.flags_any,
+                                                               q.top_k_max, q.hist, q.feed, q.feed_group, q.mask, m,
+                                                               drafts))
     if nbytes == 0:
         L.check(L.PM_ERR_UNSUPPORTED, "pm_verify_workspace_bytes")
     ws = workspace(nbytes, dev)
