@@ -16,9 +16,10 @@
 //   -- barrier: each warp takes the prefix of the tile counts (one warp
 //      scan), which places each of its tiles in the row's list;
 //   2. per owned tile: the token ids of its set bits -> the list (a lane per
-//      mask word), then a 4-byte asynchronous copy of each one's logit into
-//      its value slot, lane-strided over the positions (coalesced along runs
-//      of allowed tokens); the warp waits for its own copies;
+//      mask word);
+//   -- barrier: a 4-byte asynchronous copy of each listed logit into its
+//      value slot, position-strided over all threads (coalesced along runs
+//      of allowed tokens);
 //   3. processors on the tile's overridden ids (logit bias, penalties);
 //   -- barrier: exact tile statistics (max, integer sum of
 //      floor(e^(x - max) 2^52)): a tile with fewer than 32 allowed tokens
@@ -327,21 +328,29 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
     //    the threads' allowed counts and one shared-memory allocation of the
     //    warp's contiguous list region: every allowed token's list position
     //    is known without a CTA barrier.  Then the token ids (a whole word's
-    //    32 ids written by the warp together), 4-byte asynchronous copies of
-    //    the logits position-strided over the region (coalesced along runs
-    //    of allowed tokens), the processors and the statistics of the warp's
-    //    own tiles -- all before the first barrier.  A row whose list would
+    //    32 ids written by the warp together).  After the first barrier,
+    //    4-byte asynchronous copies of the logits position-strided over the
+    //    whole list and all 512 threads (balanced even when one warp's tiles
+    //    hold a block of allowed tokens; coalesced along runs of them), then
+    //    the processors on each warp's own tiles.  A row whose list would
     //    pass kWin positions takes the windowed path instead.
     const uint32_t* mrow = a.mask + row * a.mask_stride;
     {
+      // every load is issued before the first store waits on one: the words
+      // then cost one DRAM round trip, not one per word
       const int g0 = 32 * WPT * wid;
+      uint32_t w[kMRounds];
+#pragma unroll
+      for (int j = 0; j < kMRounds; ++j) {
+        const int g = g0 + 32 * j + lane;
+        w[j] = (j < WPT && g < nw) ? __ldcs(mrow + g) : 0u;
+      }
 #pragma unroll
       for (int j = 0; j < kMRounds; ++j) {
         if (j < WPT) {
           const int g = g0 + 32 * j + lane;
-          uint32_t w = g < nw ? __ldcs(mrow + g) : 0u;
-          if (g == nw - 1 && (a.vocab & 31)) w &= (1u << (a.vocab & 31)) - 1u;
-          mm->mw[g] = w;
+          if (g == nw - 1 && (a.vocab & 31)) w[j] &= (1u << (a.vocab & 31)) - 1u;
+          mm->mw[g] = w[j];
         }
       }
     }
@@ -367,7 +376,7 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
           if ((g & 31) == 0 && (g >> 5) < nt) mm->toff[g >> 5] = pos;  // a tile starts at this word
           const uint32_t word = my[i];
           unsigned full = __ballot_sync(kFull, word == 0xffffffffu);
-          while (full) {
+          while (full) {  // a fully allowed word: its 32 ids written by the whole warp
             const int j = __ffs(full) - 1;
             full &= full - 1;
             const int pj = __shfl_sync(kFull, pos, j);
@@ -391,28 +400,37 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
         mm->tc[t] = (lane + 1 < WPT && t + 1 < nt ? mm->toff[t + 1] : wbase + wtot) - mm->toff[t];
         clear_tile(t);
       }
-      for (int q = wbase + lane; q < wbase + wtot; q += 32) {
+    } else if (lane == 0) {
+      mm->overflow = 1;
+    }
+    __syncthreads();
+    if (mm->overflow == 0) {  // CTA-uniform
+      // the logit copies, position-strided over the whole list: every thread
+      // issues about the same number (a warp holding a block of allowed
+      // tokens would otherwise issue hundreds), coalesced along runs of
+      // allowed tokens
+      const int n_all = mm->alloc;
+      for (int q = tid; q < n_all; q += kMThreads) {
         const uint32_t id = mm->ids[q];
         cp_async4(sval + 4u * (uint32_t)q, rowp + (sizeof(T) == 4 ? id : (id & ~1u)));
       }
       cp_async_wait_all();
-      __syncwarp();
+      __syncthreads();
       if constexpr (sizeof(T) == 2) {
-        for (int q = wbase + lane; q < wbase + wtot; q += 32)
+        for (int q = tid; q < n_all; q += kMThreads)
           mm->val[q] = __float_as_uint(staged_value<T>(mm->val[q], mm->ids[q]));
-        __syncwarp();
+        __syncthreads();
       }
       if (a.bias_off || a.ovr_off) {
+        const int tw0 = WPT * wid;
         for (int t = tw0; t < tw0 + WPT && t < nt; ++t) {
           const uint32_t word = mm->mw[t * 32 + lane];
           const int pc = __popc(word);
           masked_overrides<KC>(a, p, row, t, word, warp_incl_scan(pc) - pc, mm->toff[t], mm);
         }
+        __syncthreads();
       }
-    } else if (lane == 0) {
-      mm->overflow = 1;
     }
-    __syncthreads();
     const bool fast = mm->overflow == 0;  // CTA-uniform
     const int total = fast ? mm->alloc : 0;
     // windowed path only: per tile counts (a warp sum per tile-round of the
