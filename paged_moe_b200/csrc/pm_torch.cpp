@@ -101,7 +101,7 @@ void* stream_of(const torch::Device& dev) {
 }
 
 // pm_sample_rows: [tokens, lse?, logprob?, surv_ids?, surv_probs?, n_surv?]
-// (absent outputs are empty tensors).
+// (absent outputs are empty tensors; all are views of one allocation).
 std::vector<torch::Tensor> sample_rows(torch::Tensor logits, torch::Tensor params, bool per_row, int64_t flags_any,
                                        int64_t top_k_max, OptT hist, OptT hist_len, OptT bias_tok, OptT bias_val,
                                        OptT mask, OptT forced, int64_t seed, int64_t offset, int64_t row_base,
@@ -113,29 +113,38 @@ std::vector<torch::Tensor> sample_rows(torch::Tensor logits, torch::Tensor param
                         bias_val, mask, forced);
   pm_noise nz = make_noise(seed, offset, row_base, gumbel, uniform);
   const int64_t B = r.rows;
-  auto i32 = torch::TensorOptions().dtype(torch::kInt32).device(dev);
-  auto f32 = torch::TensorOptions().dtype(torch::kFloat32).device(dev);
-  std::vector<torch::Tensor> res(6);
-  res[0] = torch::empty({B}, i32);
+  const int64_t S = survivors > 0 ? survivors : 0;
+  // every output in one device allocation (32-bit words), handed out as views
+  const int64_t words = B + (want_lse ? B : 0) + (want_logprob ? B : 0) + (S ? 2 * B * S + B : 0);
+  torch::Tensor buf = torch::empty({words}, torch::TensorOptions().dtype(torch::kInt32).device(dev));
+  torch::Tensor none = buf.narrow(0, 0, 0);
+  int64_t at = 0;
+  auto take = [&](int64_t n) {
+    torch::Tensor t = buf.narrow(0, at, n);
+    at += n;
+    return t;
+  };
+  std::vector<torch::Tensor> res(6, none);
   pm_sample_out out;
   std::memset(&out, 0, sizeof(out));
+  res[0] = take(B);
   out.tokens = res[0].data_ptr<int32_t>();
-  res[1] = want_lse ? torch::empty({B}, f32) : torch::empty({0}, f32);
-  res[2] = want_logprob ? torch::empty({B}, f32) : torch::empty({0}, f32);
-  if (want_lse) out.lse = res[1].data_ptr<float>();
-  if (want_logprob) out.token_logprob = res[2].data_ptr<float>();
-  if (survivors > 0) {
-    res[3] = torch::empty({B, survivors}, i32);
-    res[4] = torch::empty({B, survivors}, f32);
-    res[5] = torch::empty({B}, i32);
+  if (want_lse) {
+    res[1] = take(B).view(torch::kFloat32);
+    out.lse = res[1].data_ptr<float>();
+  }
+  if (want_logprob) {
+    res[2] = take(B).view(torch::kFloat32);
+    out.token_logprob = res[2].data_ptr<float>();
+  }
+  if (S) {
+    res[3] = take(B * S).view({B, S});
+    res[4] = take(B * S).view(torch::kFloat32).view({B, S});
+    res[5] = take(B);
     out.surv_ids = res[3].data_ptr<int32_t>();
     out.surv_probs = res[4].data_ptr<float>();
     out.n_surv = res[5].data_ptr<int32_t>();
-    out.surv_cap = (int32_t)survivors;
-  } else {
-    res[3] = torch::empty({0}, i32);
-    res[4] = torch::empty({0}, f32);
-    res[5] = torch::empty({0}, i32);
+    out.surv_cap = (int32_t)S;
   }
   check(pm_sample_rows(&r, &nz, &out, workspace.data_ptr(), (size_t)workspace.numel(), stream_of(dev)),
         "pm_sample_rows");
@@ -163,11 +172,14 @@ std::vector<torch::Tensor> verify(torch::Tensor logits, torch::Tensor params, bo
                         bias_val, mask, std::nullopt);
   pm_noise nz = make_noise(seed, offset, row_base, gumbel, uniform);
   const int64_t B = drafts.size(0), k = drafts.size(1);
-  auto i32 = torch::TensorOptions().dtype(torch::kInt32).device(dev);
+  // every output in one device allocation, handed out as views
+  const int64_t K1 = k + 1;
+  torch::Tensor buf = torch::empty({B * K1 + B + (want_row_tokens ? B * K1 : 0)},
+                                   torch::TensorOptions().dtype(torch::kInt32).device(dev));
   std::vector<torch::Tensor> res(3);
-  res[0] = torch::empty({B, k + 1}, i32);
-  res[1] = torch::empty({B}, i32);
-  res[2] = want_row_tokens ? torch::empty({B, k + 1}, i32) : torch::empty({0}, i32);
+  res[0] = buf.narrow(0, 0, B * K1).view({B, K1});
+  res[1] = buf.narrow(0, B * K1, B);
+  res[2] = want_row_tokens ? buf.narrow(0, B * K1 + B, B * K1).view({B, K1}) : buf.narrow(0, 0, 0);
   pm_verify_args va;
   std::memset(&va, 0, sizeof(va));
   va.mode = (int32_t)mode;

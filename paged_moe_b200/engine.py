@@ -28,8 +28,12 @@ def workspace(nbytes: int, device: torch.device, stream: Optional[torch.cuda.Str
     The kernels leave their workspace ready for the next call, so one buffer
     per stream is reused; calls on different streams get different buffers.
     """
-    stream = stream or torch.cuda.current_stream(device)
-    key = (device.index, stream.cuda_stream)
+    # the raw handle of the current stream: no Stream object per call
+    raw = stream.cuda_stream if stream is not None else torch._C._cuda_getCurrentRawStream(device.index)
+    key = (device.index, raw)
+    buf = _ws_cache.get(key)
+    if buf is not None and buf.numel() >= nbytes:
+        return buf
     with _ws_lock:
         buf = _ws_cache.get(key)
         if buf is None or buf.numel() < nbytes:
@@ -88,12 +92,16 @@ class _Keep:
         return t
 
 
+_DEFAULT_SAMPLER = SamplerSettings()
+_DEFAULT_PROCESSORS = ProcessorSettings()
+
+
 def _params_for(dev: torch.device, sampler, processors, B: int, V: int):
     """(device params tensor, flags_any, top_k_max, per_row), cached by settings."""
     single = not isinstance(sampler, (list, tuple)) and not isinstance(processors, (list, tuple))
     if single:
-        s = sampler if sampler is not None else SamplerSettings()
-        p = processors if processors is not None else ProcessorSettings()
+        s = sampler if sampler is not None else _DEFAULT_SAMPLER
+        p = processors if processors is not None else _DEFAULT_PROCESSORS
         key = (dev.index, V, s, p)
         hit = _params_cache.get(key)
         if hit is not None:
