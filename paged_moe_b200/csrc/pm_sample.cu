@@ -1812,7 +1812,8 @@ int plan_verify(const pm_rows* r, const pm_verify_args* v, VLayout* V) {
   return PM_OK;
 }
 
-// Tile statistics and log-sum-exp of the raw draft rows (no processors).
+// Tile statistics of the raw draft rows (no processors); k_accept_probs folds
+// each row's into its log-sum-exp.
 template <typename TD>
 int launch_draft_lse(const pm_rows* rows, const pm_verify_args* v, const VLayout& V, unsigned char* ws,
                      cudaStream_t st) {
@@ -1827,18 +1828,12 @@ int launch_draft_lse(const pm_rows* rows, const pm_verify_args* v, const VLayout
   da.params_per_row = 0;
   da.n_tiles = V.L.n_tiles;
   da.statx = reinterpret_cast<pm::TileStat*>(ws + V.dstat);
-  da.row_lse = reinterpret_cast<float*>(ws + V.dlse);
   const int64_t work = V.D * (int64_t)V.L.n_tiles;
   int64_t grid = (work + pm::kWarpsS - 1) / pm::kWarpsS;
   if (grid > (int64_t)num_sms() * 16) grid = (int64_t)num_sms() * 16;
   pm::k_process_rows<TD><<<(unsigned)grid, pm::kThreadsS, pm::kWarpsS * pm::kTile * 4, st>>>(da, nullptr, 0, true,
                                                                                           nullptr);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e);
-  int64_t g2 = (V.D + pm::kWarpsS - 1) / pm::kWarpsS;
-  if (g2 > (int64_t)num_sms() * 8) g2 = (int64_t)num_sms() * 8;
-  pm::k_row_lse<<<(unsigned)g2, pm::kThreadsS, 0, st>>>(da, nullptr);
-  e = cudaGetLastError();
+  const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? PM_OK : cuda_fail(e);
 }
 
@@ -2105,7 +2100,8 @@ int pm_verify(const pm_rows* rows, const pm_noise* noise, const pm_verify_args* 
   vk.dlogits = v->draft_logits;
   vk.ddtype = v->draft_dtype;
   vk.dstride = v->draft_row_stride;
-  vk.dlse = reinterpret_cast<const float*>(ws + V.dlse);
+  vk.dlse = reinterpret_cast<float*>(ws + V.dlse);
+  vk.dstat = reinterpret_cast<const pm::TileStat*>(ws + V.dstat);
   vk.u_accept = v->u_accept;
   vk.u_residual = v->u_residual;
   vk.tokens = v->tokens;

@@ -36,7 +36,8 @@ struct VerifyK {
   const void* dlogits;     // [B*k, dstride] raw draft logits
   int32_t ddtype;
   int64_t dstride;
-  const float* dlse;       // [B*k] log-sum-exp of the draft rows
+  float* dlse;             // [B*k] log-sum-exp of the draft rows (written by k_accept_probs)
+  const TileStat* dstat;   // [B*k, n_tiles] tile statistics of the draft rows
   const double* u_accept;  // [B, k] or null (Philox stream 2)
   const double* u_residual;  // [B] or null (Philox stream 3)
   int32_t* tokens;         // [B, k+1], -1 padded
@@ -129,9 +130,10 @@ __device__ __forceinline__ AccProb ld_cg_accprob(const AccProb* p) {
 }
 
 // Residual mode, before the acceptance walk: one warp per draft position
-// (request b, position i) computes p(d_i), q(d_i) and, for whole-vocabulary
-// rows, the row's log-sum-exp of y, with the same arithmetic the walk used to
-// apply position by position.
+// (request b, position i) folds the draft row's tile statistics into its
+// log-sum-exp (stored for the walk and the residual draw), then computes
+// p(d_i), q(d_i) and, for whole-vocabulary rows, the row's log-sum-exp of y,
+// with the same arithmetic the walk used to apply position by position.
 __global__ void __launch_bounds__(256) k_accept_probs(const __grid_constant__ SampleArgs a, int dtype,
                                                       const __grid_constant__ VerifyK v) {
   const int lane = threadIdx.x & 31;
@@ -145,8 +147,11 @@ __global__ void __launch_bounds__(256) k_accept_probs(const __grid_constant__ Sa
     const pm_row_params p = row_params(a, row);
     const int mode = row_mode(p);
     const int d = v.drafts[w];
+    float dm;
+    const float cd = __shfl_sync(kFull, warp_combine(v.dstat + w * a.n_tiles, a.n_tiles, &dm), 0);
+    if (lane == 0) v.dlse[w] = cd;
     AccProb r;
-    r.qd = draft_prob(v, w, d, ld_cg(&v.dlse[w]));
+    r.qd = draft_prob(v, w, d, cd);
     r.cy = 0.0f;
     r.wide = 0;
     r.pd = 0.0f;

@@ -58,10 +58,6 @@ def cached_size(key, query) -> int:
     return v
 
 
-def _shape(t: Optional[torch.Tensor]):
-    return None if t is None else tuple(t.shape)
-
-
 def _dtype_code(t: torch.Tensor) -> int:
     if t.dtype == torch.float32:
         return L.PM_DTYPE_F32
@@ -314,8 +310,8 @@ def sample_rows(logits: torch.Tensor, sampler: Union[SamplerSettings, Sequence[S
         g = keep(gumbel.to(device=dev, dtype=torch.float32).contiguous())
     if uniform is not None:
         u = keep(uniform.to(device=dev, dtype=torch.float64).contiguous())
-    key = ("sample", dev.index, tuple(q.logits.shape), q.logits.stride(0), q.logits.dtype, q.per_row, q.flags_any,
-           q.top_k_max, _shape(q.hist), _shape(q.mask))
+    key = ("sample", dev.index, q.logits.shape, q.logits.stride(0), q.logits.dtype, q.per_row, q.flags_any,
+           q.top_k_max, None if q.hist is None else q.hist.shape, None if q.mask is None else q.mask.shape)
     nbytes = cached_size(key, lambda: E.sample_workspace_bytes(q.logits, q.params, q.per_row, q.flags_any,
                                                               q.top_k_max, q.hist, q.mask))
     if nbytes == 0:

@@ -57,7 +57,8 @@ def verify(target_logits: torch.Tensor, drafts: torch.Tensor, y: torch.Tensor, s
     """
     if mode not in _MODES:
         raise ValueError(f"mode must be one of {sorted(_MODES)}")
-    drafts = torch.as_tensor(drafts)
+    if not isinstance(drafts, torch.Tensor):
+        drafts = torch.as_tensor(drafts)
     if drafts.dim() == 1:
         drafts = drafts.unsqueeze(0)
     B, k = drafts.shape
@@ -102,9 +103,9 @@ def verify(target_logits: torch.Tensor, drafts: torch.Tensor, y: torch.Tensor, s
         ur = keep(torch.as_tensor(u_residual).to(device=dev, dtype=torch.float64).reshape(B).contiguous())
     E = L.ext()
     m = _MODES[mode]
-    key = ("verify", dev.index, tuple(q.logits.shape), q.logits.stride(0), q.logits.dtype, q.per_row, q.flags_any,
-           q.top_k_max, None if q.hist is None else tuple(q.hist.shape), None if q.feed is None else tuple(q.feed.shape),
-           q.feed_group, None if q.mask is None else tuple(q.mask.shape), m, tuple(drafts.shape))
+    key = ("verify", dev.index, q.logits.shape, q.logits.stride(0), q.logits.dtype, q.per_row, q.flags_any,
+           q.top_k_max, None if q.hist is None else q.hist.shape, None if q.feed is None else q.feed.shape,
+           q.feed_group, None if q.mask is None else q.mask.shape, m, drafts.shape)
     nbytes = cached_size(key, lambda: E.verify_workspace_bytes(q.logits, q.params, q.per_row, q.flags_any,
                                                                q.top_k_max, q.hist, q.feed, q.feed_group, q.mask, m,
                                                                drafts))
