@@ -89,6 +89,42 @@ def test_masked_bf16_odd_stride_takes_the_streaming_pass():
     np.testing.assert_array_equal(res["tokens"].cpu().numpy(), ref["tokens"])
 
 
+@pytest.mark.parametrize("top_k", [20, 200])  # candidate buffers of KC = 64 and KC = 256
+def test_masked_streaming_vector_offers_after_one_value_offers(top_k):
+    """Masked bf16 rows on the streaming pass (odd row stride).  Even tiles
+    give every lane exactly 12 allowed slots (one-value offers, 384 keys, no
+    compaction), odd tiles are wholly allowed (vector offers of 256 keys at
+    once): a warp whose row part holds such a pair must make room before the
+    vector offers.  Tokens equal the oracle's."""
+    rng = np.random.default_rng(71)
+    B, V = 64, 64 * 1024
+    nt = V // 1024
+    bits = W.to_bf16_bits(W.peaked_logits(rng, B, V + 1, 2.0, 8.0, 12))
+    allowed = np.zeros((B, V), dtype=bool)
+    for t in range(1, nt, 2):
+        allowed[:, t * 1024:(t + 1) * 1024] = True
+    # lane l's slot s of a bf16 tile is element (s // 8) * 256 + 8 l + s % 8
+    slots = np.argsort(rng.random((B, nt // 2, 32, 32)), axis=-1)[..., :12]
+    lane = np.arange(32)[None, None, :, None]
+    tile = np.arange(0, nt, 2)[None, :, None, None]
+    idx = tile * 1024 + (slots // 8) * 256 + lane * 8 + slots % 8
+    np.put_along_axis(allowed, idx.reshape(B, -1), True, axis=1)
+    mask = (allowed.reshape(B, V // 32, 32).astype(np.uint64) << np.arange(32, dtype=np.uint64)).sum(2)
+    mask = mask.astype(np.uint32)
+    g = W.gumbel(rng, (B, V))
+    s = SamplerSettings(temp=0.9, top_k=top_k)
+    xf = np.ascontiguousarray(O.bf16_to_f32(bits)[:, :V])
+    ref = O.sample(xf, _osamp(s), mask=mask, gumbel=g)
+    from paged_moe_b200 import engine
+    dev = torch.device("cuda")
+    xt = torch.from_numpy(bits.view(np.int16)).to(dev).view(torch.bfloat16)[:, :V]  # row stride V + 1 (odd)
+    res = engine.sample_rows(xt, s, mask=torch.from_numpy(mask.view(np.int32)).to(dev),
+                             gumbel=torch.from_numpy(g).to(dev), return_status=True)
+    torch.cuda.synchronize()
+    assert (res["status"].cpu().numpy() == 0).all()
+    np.testing.assert_array_equal(res["tokens"].cpu().numpy(), ref["tokens"])
+
+
 def test_masked_degenerate_rows():
     """No allowed token, one allowed token, an allowed token with -inf logit."""
     rng = np.random.default_rng(34)
