@@ -85,6 +85,7 @@ struct MaskedMem {
   int overflow;                // a warp's region passed kWin: the row takes the windowed path
   int excluded;                // a finite value was left out of the selection buffer
   float v0;
+  float lse;                   // the row's log-sum-exp when an idle warp computed it during the ranking
 };
 
 // A 64-bit sum accumulated in shared memory as three 32-bit counters, one
@@ -279,6 +280,19 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
   }
   __syncthreads();
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    // the row's mask words are requested first, so their DRAM round trip
+    // overlaps the read of the row's settings; every load is issued before
+    // the first store waits on one
+    const uint32_t* mrow = a.mask + row * a.mask_stride;
+    uint32_t w[kMRounds];
+    {
+      const int g0 = 32 * WPT * wid;
+#pragma unroll
+      for (int j = 0; j < kMRounds; ++j) {
+        const int g = g0 + 32 * j + lane;
+        w[j] = (j < WPT && g < nw) ? __ldcs(mrow + g) : 0u;
+      }
+    }
     const pm_row_params p = row_params(a, row);
     const int mode = row_mode(p);
     const bool needx = needs_xstats(a, p, mode);
@@ -334,17 +348,8 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
     //    hold a block of allowed tokens; coalesced along runs of them), then
     //    the processors on each warp's own tiles.  A row whose list would
     //    pass kWin positions takes the windowed path instead.
-    const uint32_t* mrow = a.mask + row * a.mask_stride;
     {
-      // every load is issued before the first store waits on one: the words
-      // then cost one DRAM round trip, not one per word
       const int g0 = 32 * WPT * wid;
-      uint32_t w[kMRounds];
-#pragma unroll
-      for (int j = 0; j < kMRounds; ++j) {
-        const int g = g0 + 32 * j + lane;
-        w[j] = (j < WPT && g < nw) ? __ldcs(mrow + g) : 0u;
-      }
 #pragma unroll
       for (int j = 0; j < kMRounds; ++j) {
         if (j < WPT) {
@@ -472,6 +477,16 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
     for (int j = 0; j < kMaxPer; ++j)
       if (j < (wid & (kMaxPer - 1))) mine += cl[j];
 
+    // the row's log-sum-exp from the tile tree's eight warp subtrees (valid
+    // once the last window's tree is built)
+    auto row_lse = [&]() -> float {
+      const float m_row = mm->rowmax ? ord_value(mm->rowmax) : -INFINITY;
+      if (!(m_row > -INFINITY)) return -INFINITY;
+      const double z = dadd(dadd(dadd(mm->redd[0], mm->redd[1]), dadd(mm->redd[2], mm->redd[3])),
+                            dadd(dadd(mm->redd[4], mm->redd[5]), dadd(mm->redd[6], mm->redd[7])));
+      return (float)dadd((double)m_row, det_log64(dmul(z, 0x1p-52)));
+    };
+    bool lse_early = false;  // mm->lse holds the row's log-sum-exp
     int ncarry = 0;
     bool dropped = false;  // the top-K may not hold every key of the row
     uint64_t tau = 0;      // keys at or below the running K-th key cannot enter
@@ -648,6 +663,10 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
                 if (last) mm->score[rank] = fadd(fmul(key_value(kk), inv_t), row_gumbel(a, row, key_index(kk)));
               }
             }
+            // the last warp, idle while the ranking runs, computes the row's
+            // log-sum-exp (the draw then only reads it)
+            lse_early = last && needx && tot <= kMThreads - 32;  // CTA-uniform
+            if (lse_early && wid == kMWarps - 1 && lane == 0) mm->lse = row_lse();
             ncarry = tot < K ? tot : K;
             __syncthreads();
           } else {
@@ -730,15 +749,7 @@ __global__ void __launch_bounds__(kMThreads, 2) k_sample_masked(const __grid_con
     // 8. the draw (warp 0)
     if (wid == 0) {
       float c = __int_as_float(0x7fc00000);
-      if (needx) {
-        c = -INFINITY;
-        const float m_row = mm->rowmax ? ord_value(mm->rowmax) : -INFINITY;
-        if (m_row > -INFINITY) {
-          const double z = dadd(dadd(dadd(mm->redd[0], mm->redd[1]), dadd(mm->redd[2], mm->redd[3])),
-                                dadd(dadd(mm->redd[4], mm->redd[5]), dadd(mm->redd[6], mm->redd[7])));
-          c = (float)dadd((double)m_row, det_log64(dmul(z, 0x1p-52)));
-        }
-      }
+      if (needx) c = lse_early ? mm->lse : row_lse();
       int tok = 0, ns = 0;
       float x_tok = -INFINITY;
       if (mode == kGreedy) {
