@@ -9,30 +9,31 @@
 // copies, in ascending token order.  HBM traffic: the mask plus the 32-byte
 // sectors that hold an allowed token, instead of the whole row.
 //
-// Thread t loads the row's mask words t + 512 k (k < 16), so round k of warp
-// w is exactly tile w + 16 k (1024 tokens), one word per lane: warp w owns
-// the tiles w, w + 16, w + 32, ... for building the row's list.
-//   1. mask words -> shared memory; allowed count per tile (one warp sum);
-//   -- barrier: each warp takes the prefix of the tile counts (one warp
-//      scan), which places each of its tiles in the row's list;
-//   2. per owned tile: the token ids of its set bits -> the list (a lane per
-//      mask word);
+// A row whose allowed tokens fit the kWin-position list (the fast path):
+//   1. the mask words -> shared memory (coalesced loads, all issued before
+//      the first store); thread t then takes the WPT consecutive words from
+//      WPT t on, i.e. warp w the tiles [WPT w, WPT (w + 1)); one warp scan of
+//      the threads' allowed counts and one shared-memory atomic allocate the
+//      warp's list region, and the warp writes its tokens' ids there;
 //   -- barrier: a 4-byte asynchronous copy of each listed logit into its
 //      value slot, position-strided over all threads (coalesced along runs
 //      of allowed tokens);
-//   3. processors on the tile's overridden ids (logit bias, penalties);
+//   2. processors on each warp's tiles (logit bias, penalties);
 //   -- barrier: exact tile statistics (max, integer sum of
-//      floor(e^(x - max) 2^52)): a tile with fewer than 32 allowed tokens
-//      (most tiles of a sparse mask) is one thread's, serially; a denser
-//      tile is one warp's.  Each thread keeps its two largest values (and
-//      its best key, for greedy rows);
+//      floor(e^(x - max) 2^52)) over balanced runs of list positions, a pass
+//      of maxima and, after a barrier, a pass of sums; each thread keeps its
+//      largest value (and its best key, for greedy rows);
 //   -- barrier: warp 0 finds v0, a lower bound of the row's K-th largest
-//      value (the K-th largest of the threads' top two, 16-bit resolution),
+//      value (the K-th largest of the threads' maxima, 16-bit resolution),
 //      while warps 8..15 weigh one tile each for the row's log-sum-exp;
 //   -- barrier: keys >= v0 -> selection buffer (position-strided);
 //   -- barrier: every key ranked by counting the larger ones; the thread
-//      that ranks a key also computes its Gumbel score;
+//      that ranks a key also computes its Gumbel score, and the last warp,
+//      idle, the row's log-sum-exp;
 //   -- barrier: warp 0 filters and draws.
+// Windowed path: thread t's words are t + 512 k (k < 16), so round k of warp
+// w is exactly tile w + 16 k, one word per lane, and warp w builds the list
+// of tiles w, w + 16, ... of each window.
 // Rows with more than kWin allowed tokens go in windows of whole tiles (the
 // same steps per window; each window's keys are ranked together with the
 // running top-K).  Results, tie rules and noise are those of the streaming
